@@ -1,0 +1,515 @@
+"""Benchmark of the row log-sum-exp hot path on B200 (driver contract).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload fwdbwd_f32|fwd_f32|f16_vocab|intlse_q16|intlse_q10_6|sparse_f32|sparse_q16]
+
+One JSON line on rank 0.  Default workload (the headline, BASELINE metric):
+FuseLSE fp32 forward + backward over (B, N) = (512, 128256), x ~ N(0, 1),
+upstream gradient ones(B), robust mode.  One step = forward kernel + backward
+kernel over one batch already resident in HBM.  With N GPUs (torchrun, one
+process per GPU) every rank runs its own 512 rows (batch-row sharding, weak
+scaling, no collective on the data path); `value` = algorithmic bytes of all
+ranks / max-over-ranks device time.
+
+Algorithmic bytes per step and GPU (the roofline numerator):
+  forward  B*N*4 + B*4                = 262,670,336 B
+  backward 2*B*N*4 + 2*B*4            = 525,340,672 B  (read x, g, lse; write gx)
+Timing: W untimed warm-up steps; K timed steps, each bracketed by CUDA events
+on the launching stream (forward and backward separately), an L2 flush (a
+256 MiB write, > the 126 MB L2) between steps outside the events; barrier and
+synchronize around the timed region; max over ranks.
+
+`--impl reference` times the reference's own CPU implementation of the path
+(FuseLSE-CPU, fuselse/cpu/fused_fp32_cpu.cpp, built from source into
+oracle/_ref; the reference has no CPU backward, so the backward is the C
+port of grad*exp(x - lse)) on all host threads, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import shutil
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "LSE fwd+bwd HBM GB/s (% of B200 peak) at (512,128256) fp32; rows/s 1-8 GPU"
+B_ROWS, N_COLS = 512, 128256
+FALLBACK_HBM_GBS = 6650.0
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": FALLBACK_HBM_GBS, "source": "fallback"}
+
+
+def profiled_traffic(kernel: str):
+    """Per-launch DRAM bytes from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    if not p.exists():
+        return None
+    return json.loads(p.read_text()).get(kernel)
+
+
+# --------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        exe = shutil.which("nvidia-smi")
+        if exe:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                [exe, f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-f", self.path],
+                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return None
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[4:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        max_mhz = max(r[1] for r in rows)
+        loaded = [r for r in rows if r[0] > 0.5 * max_mhz] or rows
+        names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names[1:], r[2][1:]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max_mhz,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------------ workloads
+class Workload:
+    """A hot-path step on this rank's synthetic inputs."""
+    name = ""
+    config: dict = {}
+    dtype = "f32"
+    launches_per_step = 0
+
+    def kernels(self):  # [(label, callable, algorithmic bytes)]
+        raise NotImplementedError
+
+    def rows(self):
+        return 0
+
+
+class FwdBwdF32(Workload):
+    name = "fwdbwd_f32"
+    dtype = "f32"
+
+    def __init__(self, dev, seed, B=B_ROWS, N=N_COLS, do_bwd=True):
+        from fuselse_b200 import ext, workloads as W
+        self.ext, self.B, self.N, self.do_bwd = ext, B, N, do_bwd
+        self.x = W.fp32_rows(B, N, seed, dev)
+        self.g = torch.ones(B, device=dev)
+        self.lse = torch.empty(B, device=dev)
+        self.config = {"workload": f"FuseLSE fp32 {'forward+backward' if do_bwd else 'forward'} "
+                                   f"(B,N)=({B},{N}) per GPU, x~N(0,1), grad ones, robust",
+                       "B": B, "N": N, "l2": "flushed between steps (256 MiB write); input > L2",
+                       "parallelism": "batch rows, one process per GPU, no collective"}
+        self.launches_per_step = 2 if do_bwd else 1
+
+    def _fwd(self):
+        self.lse = self.ext.onepass_lse_float_robust(self.x)
+
+    def _bwd(self):
+        self.gx = self.ext.onepass_lse_float_backward(self.g, self.x, self.lse)
+
+    def kernels(self):
+        B, N = self.B, self.N
+        k = [("fwd", self._fwd, B * N * 4 + B * 4)]
+        if self.do_bwd:
+            k.append(("bwd", self._bwd, 2 * B * N * 4 + 2 * B * 4))
+        return k
+
+    def rows(self):
+        return self.B
+
+    # end to end through the public API with host buffers
+    def e2e_setup(self, dev):
+        import fuselse_b200
+        self.lse_fn = fuselse_b200.make_fuselse_logsumexp(self.ext, robust=True)
+        self.x_host = self.x.cpu().pin_memory()
+        self.g_host = self.g.cpu().pin_memory()
+        self.gx_host = torch.empty_like(self.x_host).pin_memory()
+        self.lse_host = torch.empty(self.B).pin_memory()
+        self.h2d = self.x_host.numel() * 4 + self.g_host.numel() * 4
+        self.d2h = self.gx_host.numel() * 4 + self.lse_host.numel() * 4
+
+    def e2e_step(self, dev):
+        x = self.x_host.to(dev, non_blocking=True).requires_grad_()
+        g = self.g_host.to(dev, non_blocking=True)
+        y = self.lse_fn(x, dim=-1)
+        y.backward(g)
+        self.lse_host.copy_(y.detach(), non_blocking=True)
+        self.gx_host.copy_(x.grad, non_blocking=True)
+
+
+class F16Vocab(Workload):
+    name = "f16_vocab"
+    dtype = "f16"
+
+    def __init__(self, dev, seed, world=1, rank=0):
+        from fuselse_b200 import ext, workloads as W
+        self.ext = ext
+        B, N, shards = 8192, 128256, 8
+        # this GPU's vocab shard of the (8192, 128256) logits; with fewer than 8
+        # GPUs every rank still processes one 16032-column shard per step
+        full = None
+        self.xs = W.fp16_logits(B, 16032, seed, dev)
+        self.B, self.Ns = B, self.xs.size(1)
+        self.world = world
+        self.config = {"workload": "FuseLSE16 vocab shard (8192,16032) fp16 of (8192,128256); "
+                                   "partial (max,sumexp) + NCCL all-gather + combine",
+                       "l2": "flushed between steps; input > L2"}
+        self.launches_per_step = 2
+
+    def _step(self):
+        from fuselse_b200 import distributed as D
+        ms = self.ext.lse_partial(self.xs)
+        if self.world > 1:
+            self.out = self.ext.lse_combine(D.gather_partials(ms))
+        else:
+            self.out = self.ext.lse_combine(ms.unsqueeze(0))
+
+    def kernels(self):
+        return [("partial+combine", self._step, self.B * self.Ns * 2 + self.B * 8)]
+
+    def rows(self):
+        return self.B
+
+
+class IntLSE(Workload):
+    dtype = "int32"
+
+    def __init__(self, dev, seed, kind="q16", B=16384, N=4096):
+        from fuselse_b200 import ext, workloads as W
+        self.ext, self.kind = ext, kind
+        x, q16, q106 = W.intlse_inputs(B, N, seed, dev)
+        self.q = q16 if kind == "q16" else q106
+        self.name = "intlse_" + kind
+        self.dtype = "int32" if kind == "q16" else "int16"
+        self.B, self.N = B, N
+        self.config = {"workload": f"IntLSE {kind} (B,N)=({B},{N}), x~N(0,2^2)",
+                       "l2": "flushed between steps; input > L2"}
+        self.launches_per_step = 1
+
+    def _step(self):
+        if self.kind == "q16":
+            self.out = self.ext.batched_logsumexp_q16_i32(self.q)
+        else:
+            self.out = self.ext.batched_logsumexp_q10_6(self.q)
+
+    def kernels(self):
+        return [(self.name, self._step, self.q.numel() * self.q.element_size() + self.B * 4)]
+
+    def rows(self):
+        return self.B
+
+
+class Sparse(Workload):
+    def __init__(self, dev, seed, q16=False):
+        from fuselse_b200 import ext, workloads as W
+        self.ext, self.q16 = ext, q16
+        self.args = W.sparse_layer(seed=seed, device=dev)
+        self.name = "sparse_q16" if q16 else "sparse_f32"
+        self.dtype = "int32" if q16 else "f32"
+        node, em, params, nids, cids, pids, _ = self.args
+        P, batch = em.shape
+        S, E = cids.shape
+        self.bytes = P * batch * 4 + S * batch * 4 + S * E * (8 + 8 + 4) + S * 8
+        self.S = S
+        self.config = {"workload": f"sparse PC sum layer {'Q16.16' if q16 else 'fp32'}: P={P}, S={S}, "
+                                   f"E={E}, batch={batch}", "l2": "flushed between steps"}
+        self.launches_per_step = 1
+
+    def _step(self):
+        fn = self.ext.sparse_forward_q16 if self.q16 else self.ext.sparse_forward_float
+        fn(*self.args)
+
+    def kernels(self):
+        return [(self.name, self._step, self.bytes)]
+
+    def rows(self):
+        return self.S
+
+
+def make_workload(name, dev, seed, world, rank):
+    if name == "fwdbwd_f32":
+        return FwdBwdF32(dev, seed)
+    if name == "fwd_f32":
+        return FwdBwdF32(dev, seed, do_bwd=False)
+    if name == "f16_vocab":
+        return F16Vocab(dev, seed, world, rank)
+    if name == "intlse_q16":
+        return IntLSE(dev, seed, "q16")
+    if name == "intlse_q10_6":
+        return IntLSE(dev, seed, "q10_6")
+    if name == "intlse_q16_long":
+        return IntLSE(dev, seed, "q16", B=64, N=1048576)
+    if name == "intlse_q10_6_long":
+        return IntLSE(dev, seed, "q10_6", B=64, N=1048576)
+    if name == "sparse_f32":
+        return Sparse(dev, seed, q16=False)
+    if name == "sparse_q16":
+        return Sparse(dev, seed, q16=True)
+    raise SystemExit(f"unknown workload {name}")
+
+
+# ------------------------------------------------------------------ timing
+def run_timed(wl, steps, warmup, dev, dist_on):
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    ks = wl.kernels()
+    for _ in range(warmup):
+        for _, fn, _ in ks:
+            fn()
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(ks) + 1)] for _ in range(steps)]
+    if dist_on:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    for k in range(steps):
+        flush.zero_()
+        evs[k][0].record()
+        for i, (_, fn, _) in enumerate(ks):
+            fn()
+            evs[k][i + 1].record()
+    torch.cuda.synchronize()
+    if dist_on:
+        torch.distributed.barrier()
+    per_kernel = [sum(evs[k][i].elapsed_time(evs[k][i + 1]) for k in range(steps)) / steps
+                  for i in range(len(ks))]
+    step_ms = sum(per_kernel)
+    return step_ms, per_kernel
+
+
+def run_e2e(wl, steps, warmup, dev, dist_on):
+    wl.e2e_setup(dev)
+    for _ in range(warmup):
+        wl.e2e_step(dev)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist_on:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(steps):
+        wl.e2e_step(dev)
+    e.record()
+    torch.cuda.synchronize()
+    if dist_on:
+        torch.distributed.barrier()
+    return s.elapsed_time(e) / steps
+
+
+def max_over_ranks(v, dist_on, dev):
+    if not dist_on:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------ CPU side
+def cpu_fwdbwd_step(x_np, threads):
+    """Reference FuseLSE-CPU forward (built from the reference source) + C-port backward."""
+    from oracle import oracle as O
+    if O.ref_available("ref_fused_cpu"):
+        m = O.ref_ext("ref_fused_cpu")
+        torch.set_num_threads(threads)
+        lse = m.cpu_lse_float(torch.from_numpy(x_np)).numpy()
+        kind = "reference"
+    else:
+        lse = O.fuselse_cpu_port(x_np, threads)
+        kind = "port"
+    g = np.ones(x_np.shape[0], np.float32)
+    O.lse_bwd_port(g, x_np, lse, threads)
+    return kind
+
+
+def cpu_baseline(rows, budget_s=10.0):
+    from oracle import oracle as O
+    threads = O.host_threads()
+    x = np.random.default_rng(0).standard_normal((rows, N_COLS)).astype(np.float32)
+    kind = cpu_fwdbwd_step(x, threads)  # warm-up
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        cpu_fwdbwd_step(x, threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or reps >= 50:
+            break
+    per = el / reps
+    bytes_ = 3 * rows * N_COLS * 4 + 3 * rows * 4
+    return {"value": bytes_ / per / 1e9, "unit": "GB/s", "cores": threads, "kind": kind,
+            "sample": f"fwd+bwd over ({rows},{N_COLS}) fp32 x~N(0,1), {reps} reps in {el:.1f} s; "
+                      f"fwd = reference FuseLSE-CPU (fused_fp32_cpu.cpp) at::parallel_for, "
+                      f"bwd = C port of grad*exp(x-lse), rows over {threads} threads",
+            "rows_per_s": rows / per, "cpu": _cpu_name()}
+
+
+def _cpu_name():
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    threads = O.host_threads()
+    rows = B_ROWS
+    x = np.random.default_rng(0).standard_normal((rows, N_COLS)).astype(np.float32)
+    for _ in range(args.warmup):
+        kind = cpu_fwdbwd_step(x, threads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        kind = cpu_fwdbwd_step(x, threads)
+        times.append(time.perf_counter() - t0)
+    per = sum(times) / len(times)
+    bytes_ = 3 * rows * N_COLS * 4 + 3 * rows * 4
+    value = bytes_ / per / 1e9
+    line = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": f"FuseLSE fp32 forward+backward (B,N)=({rows},{N_COLS}) on host CPU",
+                       "B": rows, "N": N_COLS},
+            "rows_per_s": rows / per,
+            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": kind,
+                             "sample": f"full ({rows},{N_COLS}) fwd+bwd per step; fwd = reference "
+                                       "FuseLSE-CPU built from source, bwd = C port (the reference "
+                                       "has no CPU backward)", "cpu": _cpu_name()},
+            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="fwdbwd_f32")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist_on = world > 1
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if dist_on:
+        from datetime import timedelta
+        torch.distributed.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+
+    wl = make_workload(args.workload, dev, seed=rank, world=world, rank=rank)
+    with ClockSampler(local) as clk:
+        step_ms, per_kernel = run_timed(wl, args.steps, args.warmup, dev, dist_on)
+    clocks = clk.summary()
+    step_ms = max_over_ranks(step_ms, dist_on, dev)
+    per_kernel = [max_over_ranks(v, dist_on, dev) for v in per_kernel]
+    ks = wl.kernels()
+    bytes_step = sum(b for _, _, b in ks)
+    value = world * bytes_step / (step_ms * 1e-3) / 1e9
+    peaks = measured_peaks()
+
+    # dominant kernel roofline
+    i_dom = int(np.argmax(per_kernel))
+    lab, _, b_dom = ks[i_dom]
+    ach = b_dom / (per_kernel[i_dom] * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "kernel": lab, "achieved": ach, "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": ach / peaks["hbm_gbs"], "peak_source": peaks["source"],
+                "traffic": profiled_traffic(lab)}
+    kernels = {l: {"ms": t, "algorithmic_bytes": b, "GB_s": b / (t * 1e-3) / 1e9,
+                   "frac_of_peak": b / (t * 1e-3) / 1e9 / peaks["hbm_gbs"]}
+               for (l, _, b), t in zip(ks, per_kernel)}
+
+    e2e = None
+    if not args.no_e2e and hasattr(wl, "e2e_step"):
+        e2e_ms = max_over_ranks(run_e2e(wl, max(3, args.steps // 4), 3, dev, dist_on), dist_on, dev)
+        e2e = {"value": world * bytes_step / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
+               "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h, "ms_per_step": e2e_ms}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "fwdbwd_f32":
+        try:
+            cpu = cpu_baseline(rows=B_ROWS)
+        except Exception as exc:  # the baseline is reported, never required
+            cpu = {"value": None, "error": repr(exc)}
+
+    if rank == 0:
+        line = {"metric": METRIC if args.workload == "fwdbwd_f32" else f"{wl.name} HBM GB/s",
+                "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
+                "config": dict(wl.config, parallelism=f"rows x{world}" if world > 1 else "1 GPU"),
+                "rows_per_s": world * wl.rows() / (step_ms * 1e-3),
+                "pct_of_peak": 100.0 * value / (world * peaks["hbm_gbs"]),
+                "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu, "e2e": e2e,
+                "clocks": clocks, "gpu_launches": wl.launches_per_step * args.steps,
+                "gpu": torch.cuda.get_device_name(dev)}
+        print(json.dumps(line), flush=True)
+    if dist_on:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,85 @@
+"""Build recipe for libfuselse_b200.so (sm_100a), in-tree.
+
+    python -m fuselse_b200.build [--verbose]
+
+Each csrc/*.cu is compiled with nvcc for `-gencode arch=compute_100a,code=sm_100a`
+into build objects under fuselse_b200/_build/, then linked into
+fuselse_b200/libfuselse_b200.so (CUDA runtime linked statically, so the
+library only needs the driver).  Objects are rebuilt when their source or a
+header changed.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+CSRC = PKG / "csrc"
+BUILD = PKG / "_build"
+LIB = PKG / "libfuselse_b200.so"
+HEADERS = [ROOT / "include" / "fuselse_b200.h", *sorted(CSRC.glob("*.cuh"))]
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O2", "-I", str(ROOT / "include")]
+# Per-file extra flags.  sparse.cu matches the reference kernels' fast-math
+# build so its log-weights and Q16.16 conversions round identically.
+EXTRA = {"sparse.cu": ["--use_fast_math"]}
+
+
+def nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and Path(cand).exists():
+            return cand
+    raise RuntimeError("nvcc not found: set NVCC or put CUDA's bin on PATH")
+
+
+def _stale(obj: Path, src: Path) -> bool:
+    if not obj.exists():
+        return True
+    t = obj.stat().st_mtime
+    return any(p.stat().st_mtime > t for p in [src, *HEADERS])
+
+
+def build(verbose: bool = False, ptxas_info: bool = False) -> Path:
+    BUILD.mkdir(exist_ok=True)
+    cc = nvcc()
+    objs = []
+    for src in sorted(CSRC.glob("*.cu")):
+        obj = BUILD / (src.stem + ".o")
+        objs.append(obj)
+        if not _stale(obj, src) and not ptxas_info:
+            continue
+        cmd = [cc, *ARCH, *COMMON, *EXTRA.get(src.name, []), "-c", str(src), "-o", str(obj)]
+        if ptxas_info:
+            cmd.insert(1, "-Xptxas=-v")
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0 or verbose or ptxas_info:
+            sys.stderr.write(r.stdout + r.stderr)
+        if r.returncode != 0:
+            raise RuntimeError(f"nvcc failed on {src.name}")
+    if not LIB.exists() or any(o.stat().st_mtime > LIB.stat().st_mtime for o in objs):
+        tmp = LIB.with_suffix(".so.tmp")
+        cmd = [cc, *ARCH, "-shared", "-Xcompiler", "-fPIC", "-o", str(tmp), *map(str, objs)]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            sys.stderr.write(r.stdout + r.stderr)
+            raise RuntimeError("linking libfuselse_b200.so failed")
+        os.replace(tmp, LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--verbose", action="store_true")
+    ap.add_argument("--ptxas-info", action="store_true", help="print registers / spills per kernel")
+    args = ap.parse_args()
+    print(build(verbose=args.verbose, ptxas_info=args.ptxas_info))

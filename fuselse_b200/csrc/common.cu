@@ -1,0 +1,69 @@
+// Host-side plumbing shared by every entry point: per-thread error
+// messages, device binding from a stream or pointer, SM count cache.
+#include "common.cuh"
+
+#include <mutex>
+
+namespace fl {
+
+static thread_local std::string g_last_error;
+
+void set_error(const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+}
+
+void clear_error() { g_last_error.clear(); }
+
+int bind_device(fl_stream_t stream, const void* ptr) {
+    int dev = -1;
+    if (stream != nullptr) {
+        FL_CUDA(cudaStreamGetDevice(reinterpret_cast<cudaStream_t>(stream), &dev));
+    } else if (ptr != nullptr) {
+        cudaPointerAttributes attr;
+        FL_CUDA(cudaPointerGetAttributes(&attr, ptr));
+        if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged) {
+            set_error("pointer %p is not device memory", ptr);
+            return FL_ERR_INVALID_ARGUMENT;
+        }
+        dev = attr.device;
+    } else {
+        FL_CUDA(cudaGetDevice(&dev));
+    }
+    int cur = -1;
+    FL_CUDA(cudaGetDevice(&cur));
+    if (cur != dev) FL_CUDA(cudaSetDevice(dev));
+    return FL_OK;
+}
+
+int sm_count() {
+    static int cache[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return kNumSMs;
+    if (cache[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+            n = kNumSMs;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
+int check_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        set_error("%s: launch failed: %s", what, cudaGetErrorString(e));
+        return FL_ERR_CUDA;
+    }
+    return FL_OK;
+}
+
+}  // namespace fl
+
+extern "C" const char* fl_last_error(void) { return fl::g_last_error.c_str(); }
+
+extern "C" int fl_version(void) { return 100; }  // 0.1.0

@@ -1,0 +1,129 @@
+// Shared host/device helpers for the fuselse_b200 kernels (sm_100a only).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cstdio>
+#include <cstdarg>
+#include <string>
+
+#include "../../include/fuselse_b200.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "fuselse_b200 targets sm_100a only"
+#endif
+
+namespace fl {
+
+constexpr int kNumSMs = 148;  // B200; the host queries the real count once
+
+// ---------------------------------------------------------------------------
+// Host-side status handling: a thread-local message per failed call.
+// ---------------------------------------------------------------------------
+void set_error(const char* fmt, ...);
+void clear_error();
+
+// Makes the device that owns `stream` (or, for the NULL stream, `ptr`)
+// current for this host thread in this library's CUDA runtime instance.
+// Returns FL_OK or FL_ERR_CUDA.
+int bind_device(fl_stream_t stream, const void* ptr);
+
+int sm_count();  // of the current device, cached per device
+
+// Launch-error check after a kernel launch.
+int check_launch(const char* what);
+
+#define FL_REQUIRE(cond, ...)                                  \
+    do {                                                       \
+        if (!(cond)) {                                         \
+            ::fl::set_error(__VA_ARGS__);                      \
+            return FL_ERR_INVALID_ARGUMENT;                    \
+        }                                                      \
+    } while (0)
+
+#define FL_CUDA(call)                                                        \
+    do {                                                                     \
+        cudaError_t _e = (call);                                             \
+        if (_e != cudaSuccess) {                                             \
+            ::fl::set_error("%s failed: %s", #call, cudaGetErrorString(_e)); \
+            return FL_ERR_CUDA;                                              \
+        }                                                                    \
+    } while (0)
+
+inline bool aligned_to(const void* p, size_t a) {
+    return (reinterpret_cast<uintptr_t>(p) % a) == 0;
+}
+
+// ---------------------------------------------------------------------------
+// Device helpers
+// ---------------------------------------------------------------------------
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// 16-byte streaming load: read-only path, no L1 allocation, 256-byte L2
+// prefetch granule (rows are read once, front to back).
+__device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
+    uint4 v;
+    asm volatile(
+        "ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+        : "l"(p));
+    return v;
+}
+
+// 16-byte store that marks the lines evict-first in L2 (written once).
+__device__ __forceinline__ void st_stream_f4(void* p, float4 v) {
+    asm volatile("st.global.cs.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p),
+                 "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+
+// Hardware base-2 exponential (MUFU.EX2), denormal results flushed.
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// max that propagates NaN (PTX max.NaN.f32, sm_80+).
+__device__ __forceinline__ float max_nan(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+
+// ---------------------------------------------------------------------------
+// Online log-sum-exp state (m, s): m = running max (NaN-propagating),
+// s = sum exp(x - safe(m)), safe(-inf) = 0 so an all--inf prefix keeps s = 0.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float safe_max(float m) {
+    return m == -INFINITY ? 0.0f : m;
+}
+
+// Merge (m2, s2) into (m, s).
+__device__ __forceinline__ void ms_merge(float& m, float& s, float m2, float s2) {
+    const float M = max_nan(m, m2);
+    const float Ml = safe_max(M) * kLog2e;
+    s = s * ex2(fmaf(m, kLog2e, -Ml)) + s2 * ex2(fmaf(m2, kLog2e, -Ml));
+    m = M;
+}
+
+// Final value of a state under the robust IEEE rules.
+__device__ __forceinline__ float ms_finalize(float m, float s, float empty_value) {
+    if (m != m) return m;                 // NaN anywhere
+    if (m == INFINITY) return INFINITY;   // +inf (and no NaN)
+    if (m == -INFINITY) return empty_value;  // empty or all -inf
+    return m + logf(s);
+}
+
+// Warp-wide merge of (m, s) with xor butterflies; every lane ends with the total.
+__device__ __forceinline__ void ms_warp_allreduce(float& m, float& s) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
+        const float s2 = __shfl_xor_sync(0xffffffffu, s, off);
+        ms_merge(m, s, m2, s2);
+    }
+}
+
+}  // namespace fl

@@ -1,0 +1,289 @@
+// IntLSE row kernels (Q16.16 from fp32 or int32, Q10.6 from int16), bit-identical
+// to intlse/gpu/lse_kernel.cu:67-159 and intlse/gpu/lse_kernel_q10_6.cu:55-139.
+//
+// The pair op is not associative, so the reduction order is the contract:
+// each row is reduced by 256 "chains" exactly as the reference's 256 threads
+// do it — chain t takes head element t (elements before the first 16-byte
+// (Q16) / 8-byte (Q10.6) boundary of the row), then vectors t, t+256, ...
+// (4 elements each, in order), then tail element t; the first element seeds
+// the chain, an empty chain holds -0x3fffffff; the 32 chains of a warp are
+// merged by xor butterflies (offsets 16..1), and the 8 warp values, padded to
+// 32 lanes with -0x3fffffff, by a second butterfly.
+//
+// What is B200-specific is everything around that order:
+//   * the 256 chains of a row may be spread over a cluster of 1/2/4/8 CTAs
+//     (so 64 long rows still occupy every SM), warp values meeting in the
+//     leader CTA's shared memory through DSMEM;
+//   * the correction table lives in shared memory replicated per lane
+//     (conflict-free) instead of __constant__ with divergent indices;
+//   * the pair step is the shorter-chain restatement of intlse.cuh, and the
+//     table read is skipped for a whole warp when no lane can need it;
+//   * each chain keeps D vectors of its row in flight in registers.
+#include "common.cuh"
+#include "intlse.cuh"
+
+#include <cooperative_groups.h>
+
+namespace cg = cooperative_groups;
+
+namespace fl {
+namespace {
+
+enum Kind { kQ16F32 = 0, kQ16I32 = 1, kQ106I16 = 2 };
+
+// Reference constants (lse_kernel.cu:23-27): CONV = LOG2_E * 2^16 and
+// LN_2 / 2^16 from the same decimal literals, so the float values match.
+constexpr float kRefLog2e = 1.44269504089f;
+constexpr float kRefLn2 = 0.69314718056f;
+constexpr float kConvQ16 = kRefLog2e * 65536.0f;
+constexpr float kOutQ16 = kRefLn2 / 65536.0f;
+constexpr float kOutQ106 = kRefLn2 / 64.0f;
+
+template <int KIND>
+struct IK;
+
+template <>
+struct IK<kQ16F32> {
+    using In = float;
+    static constexpr int F = 16, VB = 16;
+    __device__ __forceinline__ static int conv(uint32_t bits) {
+        return __float2int_rn(__fmul_rn(__uint_as_float(bits), kConvQ16));
+    }
+    __device__ __forceinline__ static int load1(const In* p) {
+        return conv(__float_as_uint(__ldg(p)));
+    }
+};
+
+template <>
+struct IK<kQ16I32> {
+    using In = int32_t;
+    static constexpr int F = 16, VB = 16;
+    __device__ __forceinline__ static int conv(uint32_t bits) { return (int)bits; }
+    __device__ __forceinline__ static int load1(const In* p) { return __ldg(p); }
+};
+
+template <>
+struct IK<kQ106I16> {
+    using In = int16_t;
+    static constexpr int F = 6, VB = 8;
+    __device__ __forceinline__ static int load1(const In* p) { return (int)__ldg(p); }
+};
+
+// One vector of 4 elements already widened to int32 chain values.
+struct Q4 {
+    int v[4];
+};
+
+template <int KIND>
+__device__ __forceinline__ Q4 load_vec(const typename IK<KIND>::In* base, int64_t i) {
+    Q4 q;
+    if constexpr (KIND == kQ106I16) {
+        uint32_t a, b;
+        asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+                     : "=r"(a), "=r"(b)
+                     : "l"(base + 4 * i));
+        q.v[0] = (int)(int16_t)(a & 0xffffu);
+        q.v[1] = (int)a >> 16;
+        q.v[2] = (int)(int16_t)(b & 0xffffu);
+        q.v[3] = (int)b >> 16;
+    } else {
+        const uint4 r = ld_stream_u4(base + 4 * i);
+        q.v[0] = IK<KIND>::conv(r.x);
+        q.v[1] = IK<KIND>::conv(r.y);
+        q.v[2] = IK<KIND>::conv(r.z);
+        q.v[3] = IK<KIND>::conv(r.w);
+    }
+    return q;
+}
+
+template <int KIND>
+__device__ __forceinline__ int64_t head_count(const typename IK<KIND>::In* rowp, int64_t N) {
+    using In = typename IK<KIND>::In;
+    constexpr uint32_t VB = IK<KIND>::VB;
+    const uint32_t mis = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(rowp) & (VB - 1));
+    const int64_t h = mis ? static_cast<int64_t>((VB - mis) / sizeof(In)) : 0;
+    return h < N ? h : N;
+}
+
+template <int F>
+__device__ __forceinline__ float to_output(int acc) {
+    return __fmul_rn(__int2float_rn(acc), F == 16 ? kOutQ16 : kOutQ106);
+}
+
+// CTA threads run the chains [rank*CTA, rank*CTA + CTA) of one row.
+template <int KIND, bool LUT, int CTA, int D>
+__global__ void __launch_bounds__(CTA) intlse_rows_kernel(
+    const typename IK<KIND>::In* __restrict__ x, float* __restrict__ out, int64_t N) {
+    using In = typename IK<KIND>::In;
+    constexpr int F = IK<KIND>::F;
+    constexpr int C = 256 / CTA;
+    __shared__ int lut_s[64 * 32];
+    __shared__ int warp_val[8];
+
+    const int rank = C > 1 ? static_cast<int>(blockIdx.x % C) : 0;
+    const int64_t row = blockIdx.x / C;
+    const int lane = threadIdx.x & 31;
+    const int t = rank * CTA + threadIdx.x;
+
+    if constexpr (LUT) {
+        const int* src = F == 16 ? kLutQ16 : kLutQ10_6;
+        for (int i = threadIdx.x; i < 64 * 32; i += CTA) lut_s[i] = src[i >> 5];
+        __syncthreads();
+    }
+    const LaneLut lut{lut_s + lane};
+
+    const In* rowp = x + row * N;
+    const int64_t head = head_count<KIND>(rowp, N);
+    const int64_t nv = (N - head) / 4;
+    const int64_t tail0 = head + nv * 4;
+    const int64_t K = (nv + 255) / 256;  // vector steps, uniform over the row
+    const In* vbase = rowp + head;
+
+    int acc = kQNegInf;
+    bool has = false;
+    if (t < head) {
+        acc = IK<KIND>::load1(rowp + t);
+        has = true;
+    }
+    // vector step 0 carries the seed when there was no head element
+    if (t < nv) {
+        const Q4 q = load_vec<KIND>(vbase, t);
+        acc = has ? pair_exact<F, LUT>(acc, q.v[0], lut) : q.v[0];
+        has = true;
+#pragma unroll
+        for (int e = 1; e < 4; ++e) acc = pair_exact<F, LUT>(acc, q.v[e], lut);
+    }
+    // steps 1..K-1: every lane of a chain that is active here already has a seed
+    {
+        Q4 buf[D];
+#pragma unroll
+        for (int d = 0; d < D; ++d) {
+            const int64_t i = (int64_t)(1 + d) * 256 + t;
+            if (1 + d < K && i < nv) buf[d] = load_vec<KIND>(vbase, i);
+        }
+        for (int64_t k0 = 1; k0 < K; k0 += D) {
+#pragma unroll
+            for (int d = 0; d < D; ++d) {
+                const int64_t k = k0 + d;
+                if (k < K) {
+                    const Q4 cur = buf[d];
+                    const int64_t in = (k + D) * 256 + t;
+                    if (k + D < K && in < nv) buf[d] = load_vec<KIND>(vbase, in);
+                    const bool active = k * 256 + t < nv;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) pair_warp<F, LUT>(acc, cur.v[e], active, lut);
+                }
+            }
+        }
+    }
+    if (tail0 + t < N) {
+        const int q = IK<KIND>::load1(rowp + tail0 + t);
+        acc = has ? pair_exact<F, LUT>(acc, q, lut) : q;
+    }
+
+    // warp butterfly (reference lse_kernel.cu:116-119)
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+        acc = pair_exact<F, LUT>(acc, __shfl_xor_sync(0xffffffffu, acc, off), lut);
+
+    if constexpr (C > 1) {
+        cg::cluster_group cluster = cg::this_cluster();
+        if (lane == 0) {
+            int* dst = cluster.map_shared_rank(warp_val, 0);
+            dst[t >> 5] = acc;
+        }
+        cluster.sync();
+        if (rank != 0) return;
+    } else {
+        if (lane == 0) warp_val[t >> 5] = acc;
+        __syncthreads();
+    }
+    // second butterfly over the 8 warp values padded to 32 lanes (:122-132)
+    if (threadIdx.x < 32) {
+        int v = lane < 8 ? warp_val[lane] : kQNegInf;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1)
+            v = pair_exact<F, LUT>(v, __shfl_xor_sync(0xffffffffu, v, off), lut);
+        if (lane == 0) out[row] = to_output<F>(v);
+    }
+}
+
+template <int KIND, bool LUT, int CTA, int D>
+int launch_cfg(const typename IK<KIND>::In* x, float* out, int64_t B, int64_t N,
+               cudaStream_t stream) {
+    constexpr int C = 256 / CTA;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(B * C));
+    cfg.blockDim = dim3(CTA);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = C;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    FL_CUDA(cudaLaunchKernelEx(&cfg, intlse_rows_kernel<KIND, LUT, CTA, D>, x, out, N));
+    return FL_OK;
+}
+
+template <int KIND, bool LUT, int D>
+int launch_d(const typename IK<KIND>::In* x, float* out, int64_t B, int64_t N, int C,
+             cudaStream_t stream) {
+    switch (C) {
+        case 8: return launch_cfg<KIND, LUT, 32, D>(x, out, B, N, stream);
+        case 4: return launch_cfg<KIND, LUT, 64, D>(x, out, B, N, stream);
+        case 2: return launch_cfg<KIND, LUT, 128, D>(x, out, B, N, stream);
+        default: return launch_cfg<KIND, LUT, 256, D>(x, out, B, N, stream);
+    }
+}
+
+template <int KIND, bool LUT>
+int launch_intlse(const typename IK<KIND>::In* x, float* out, int64_t B, int64_t N,
+                  fl_stream_t stream, const char* what) {
+    using In = typename IK<KIND>::In;
+    FL_REQUIRE(B >= 0 && N >= 0, "%s: negative shape", what);
+    FL_REQUIRE(B == 0 || out != nullptr, "%s: out is NULL", what);
+    FL_REQUIRE(B == 0 || N == 0 || x != nullptr, "%s: x is NULL", what);
+    FL_REQUIRE(aligned_to(x, sizeof(In)) && aligned_to(out, 4), "%s: misaligned buffer", what);
+    FL_REQUIRE(N <= (int64_t)INT32_MAX, "%s: N=%lld exceeds the reference's int row length", what,
+               (long long)N);
+    if (B == 0) return FL_OK;
+    if (int st = bind_device(stream, out)) return st;
+    // spread a row's 256 chains over up to 8 CTAs when rows are scarce
+    const int64_t sms = sm_count();
+    int C = 1;
+    while (C < 8 && B * C < 4 * sms) C *= 2;
+    FL_REQUIRE(B * C <= (int64_t)INT32_MAX, "%s: B=%lld too large", what, (long long)B);
+    const int64_t K = (N / 4 + 255) / 256;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    int st = K > 8 ? launch_d<KIND, LUT, 16>(x, out, B, N, C, s)
+                   : launch_d<KIND, LUT, 4>(x, out, B, N, C, s);
+    if (st) return st;
+    return check_launch(what);
+}
+
+}  // namespace
+}  // namespace fl
+
+using namespace fl;
+
+extern "C" int fl_intlse_q16_f32(const float* x, float* out, int64_t B, int64_t N, int use_lut,
+                                 fl_stream_t stream) {
+    clear_error();
+    return use_lut ? launch_intlse<kQ16F32, true>(x, out, B, N, stream, "fl_intlse_q16_f32")
+                   : launch_intlse<kQ16F32, false>(x, out, B, N, stream, "fl_intlse_q16_f32");
+}
+
+extern "C" int fl_intlse_q16_i32(const int32_t* q, float* out, int64_t B, int64_t N,
+                                 int use_lut, fl_stream_t stream) {
+    clear_error();
+    return use_lut ? launch_intlse<kQ16I32, true>(q, out, B, N, stream, "fl_intlse_q16_i32")
+                   : launch_intlse<kQ16I32, false>(q, out, B, N, stream, "fl_intlse_q16_i32");
+}
+
+extern "C" int fl_intlse_q10_6_i16(const int16_t* q, float* out, int64_t B, int64_t N,
+                                   fl_stream_t stream) {
+    clear_error();
+    return launch_intlse<kQ106I16, true>(q, out, B, N, stream, "fl_intlse_q10_6_i16");
+}

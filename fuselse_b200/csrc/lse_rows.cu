@@ -1,0 +1,450 @@
+// FuseLSE row reductions for sm_100a: fp32 / fp16 forward, per-shard
+// partial states with their combine, and the fp32 backward.
+//
+// Forward design (replaces the one-block-per-row pairwise reduction of
+// fuselse/gpu/fused_fp32_kernel.cu:50-133 and fused_fp16_kernel.cu:25-110):
+//   * online (max, sum-exp) state per thread: one MUFU.EX2 per element instead
+//     of the reference's exp + log pair per element;
+//   * 16-byte streaming loads (ld.global.nc, no L1 allocation, 256 B L2
+//     prefetch), U vectors in flight per thread;
+//   * long rows are split into `nseg` contiguous segments, one CTA each, the
+//     CTAs of a row forming a thread-block cluster whose partial states are
+//     merged through distributed shared memory (no global scratch, one launch);
+//   * short rows go one warp per row (8 rows per 256-thread CTA).
+// Backward (replaces logsumexp_float_backward_kernel, fused_fp32_kernel.cu:135-150):
+//   row-chunked grid (no per-element division), 16-byte load + 16-byte
+//   evict-first store per 4 elements, exp as FFMA + EX2.
+#include "common.cuh"
+
+#include <cooperative_groups.h>
+#include <cuda_fp16.h>
+#include <algorithm>
+#include <cstdlib>
+
+namespace cg = cooperative_groups;
+
+namespace fl {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kMaxSeg = 8;  // portable cluster size
+
+// Element traits: how many elements one 16-byte vector carries and how to
+// widen them to fp32.
+template <typename T>
+struct Elem;
+
+template <>
+struct Elem<float> {
+    static constexpr int kPerVec = 4;
+    __device__ __forceinline__ static float load1(const float* p) { return __ldg(p); }
+    __device__ __forceinline__ static void unpack(uint4 r, float* v) {
+        v[0] = __uint_as_float(r.x);
+        v[1] = __uint_as_float(r.y);
+        v[2] = __uint_as_float(r.z);
+        v[3] = __uint_as_float(r.w);
+    }
+};
+
+template <>
+struct Elem<__half> {
+    static constexpr int kPerVec = 8;
+    __device__ __forceinline__ static float load1(const __half* p) { return __half2float(__ldg(p)); }
+    __device__ __forceinline__ static void unpack(uint4 r, float* v) {
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+            float2 f = __half22float2(h);
+            v[2 * i] = f.x;
+            v[2 * i + 1] = f.y;
+        }
+    }
+};
+
+// Fold K values into the thread state (m, s): one max tree, one rescale,
+// K EX2s summed into two partial accumulators.
+template <int K>
+__device__ __forceinline__ void ms_fold(float& m, float& s, const float* v) {
+    float t[K];
+#pragma unroll
+    for (int i = 0; i < K; ++i) t[i] = v[i];
+#pragma unroll
+    for (int w = 1; w < K; w *= 2)
+#pragma unroll
+        for (int i = 0; i + w < K; i += 2 * w) t[i] = max_nan(t[i], t[i + w]);
+    const float M = max_nan(m, t[0]);
+    const float Ml = safe_max(M) * kLog2e;
+    float a0 = s * ex2(fmaf(m, kLog2e, -Ml));
+    float a1 = 0.0f;
+#pragma unroll
+    for (int i = 0; i < K; i += 2) {
+        a0 += ex2(fmaf(v[i], kLog2e, -Ml));
+        if (i + 1 < K) a1 += ex2(fmaf(v[i + 1], kLog2e, -Ml));
+    }
+    s = a0 + a1;
+    m = M;
+}
+
+__device__ __forceinline__ void ms_fold1(float& m, float& s, float v) {
+    ms_merge(m, s, v, v == -INFINITY ? 0.0f : 1.0f);
+}
+
+// Misalignment prefix: elements before the first 16-byte boundary of a row.
+template <typename T>
+__device__ __forceinline__ int64_t head_elems(const T* rowp, int64_t N) {
+    const uint32_t mis = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(rowp) & 15u);
+    int64_t p = mis ? static_cast<int64_t>((16u - mis) / sizeof(T)) : 0;
+    return p < N ? p : N;
+}
+
+// Accumulate vectors [v0, v1) of a row (vector i starts at element head + i*E)
+// with `stride` threads, this thread starting at `first`.
+template <typename T, int U>
+__device__ __forceinline__ void fold_vectors(const T* vbase, int64_t v0, int64_t v1,
+                                             int first, int stride, float& m, float& s) {
+    constexpr int E = Elem<T>::kPerVec;
+    const uint4* vp = reinterpret_cast<const uint4*>(vbase);
+    int64_t i = v0 + first;
+    for (; i + (int64_t)(U - 1) * stride < v1; i += (int64_t)U * stride) {
+        uint4 r[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) r[u] = ld_stream_u4(vp + i + (int64_t)u * stride);
+        float v[U * E];
+#pragma unroll
+        for (int u = 0; u < U; ++u) Elem<T>::unpack(r[u], v + u * E);
+        ms_fold<U * E>(m, s, v);
+    }
+    for (; i < v1; i += stride) {
+        float v[E];
+        Elem<T>::unpack(ld_stream_u4(vp + i), v);
+        ms_fold<E>(m, s, v);
+    }
+}
+
+// Block-wide merge; the result is valid in thread 0.
+__device__ __forceinline__ void ms_block_reduce(float& m, float& s) {
+    __shared__ float2 part[kWarps];
+    ms_warp_allreduce(m, s);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) part[warp] = make_float2(m, s);
+    __syncthreads();
+    if (warp == 0) {
+        float2 p = lane < kWarps ? part[lane] : make_float2(-INFINITY, 0.0f);
+        m = p.x;
+        s = p.y;
+#pragma unroll
+        for (int off = kWarps / 2; off > 0; off >>= 1) {
+            const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
+            const float s2 = __shfl_xor_sync(0xffffffffu, s, off);
+            ms_merge(m, s, m2, s2);
+        }
+    }
+}
+
+// One CTA per row segment; the nseg CTAs of a row form one cluster.
+// PARTIAL: write (m, s) pairs instead of the finished value.
+template <typename T, bool PARTIAL, int U>
+__global__ void __launch_bounds__(kThreads) lse_segment_kernel(
+    const T* __restrict__ x, float* __restrict__ out, int64_t B, int64_t N,
+    int nseg, float empty_value) {
+    constexpr int E = Elem<T>::kPerVec;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = static_cast<int>(blockIdx.x % nseg);
+    const int64_t row = blockIdx.x / nseg;
+    __shared__ float2 seg_part[kMaxSeg];
+
+    float m = -INFINITY, s = 0.0f;
+    if (row < B) {
+        const T* rowp = x + row * N;
+        const int64_t head = head_elems(rowp, N);
+        const int64_t nv = (N - head) / E;
+        const int64_t tail0 = head + nv * E;
+        const int64_t per = (nv + nseg - 1) / nseg;
+        const int64_t v0 = min(nv, per * rank), v1 = min(nv, v0 + per);
+        fold_vectors<T, U>(rowp + head, v0, v1, threadIdx.x, kThreads, m, s);
+        if (rank == 0) {
+            // at most E-1 head and E-1 tail elements
+            if (threadIdx.x < head) ms_fold1(m, s, Elem<T>::load1(rowp + threadIdx.x));
+            if (tail0 + threadIdx.x < N) ms_fold1(m, s, Elem<T>::load1(rowp + tail0 + threadIdx.x));
+        }
+    }
+    ms_block_reduce(m, s);
+    if (nseg > 1) {
+        if (threadIdx.x == 0) {
+            float2* dst = cluster.map_shared_rank(seg_part, 0);
+            dst[rank] = make_float2(m, s);
+        }
+        cluster.sync();
+        if (rank != 0) return;
+        if (threadIdx.x == 0) {
+            m = seg_part[0].x;
+            s = seg_part[0].y;
+            for (int r = 1; r < nseg; ++r) ms_merge(m, s, seg_part[r].x, seg_part[r].y);
+        }
+    }
+    if (threadIdx.x == 0 && row < B) {
+        if (PARTIAL) {
+            reinterpret_cast<float2*>(out)[row] = make_float2(m, s);
+        } else {
+            out[row] = ms_finalize(m, s, empty_value);
+        }
+    }
+}
+
+// One warp per row for short rows.
+template <typename T, bool PARTIAL, int U>
+__global__ void __launch_bounds__(kThreads) lse_warp_kernel(
+    const T* __restrict__ x, float* __restrict__ out, int64_t B, int64_t N,
+    float empty_value) {
+    constexpr int E = Elem<T>::kPerVec;
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+    if (row >= B) return;
+    const T* rowp = x + row * N;
+    const int64_t head = head_elems(rowp, N);
+    const int64_t nv = (N - head) / E;
+    const int64_t tail0 = head + nv * E;
+    float m = -INFINITY, s = 0.0f;
+    fold_vectors<T, U>(rowp + head, 0, nv, lane, 32, m, s);
+    if (lane < head) ms_fold1(m, s, Elem<T>::load1(rowp + lane));
+    if (tail0 + lane < N) ms_fold1(m, s, Elem<T>::load1(rowp + tail0 + lane));
+    ms_warp_allreduce(m, s);
+    if (lane == 0) {
+        if (PARTIAL) {
+            reinterpret_cast<float2*>(out)[row] = make_float2(m, s);
+        } else {
+            out[row] = ms_finalize(m, s, empty_value);
+        }
+    }
+}
+
+__global__ void lse_combine_kernel(const float2* __restrict__ ms, float* __restrict__ out,
+                                   int64_t G, int64_t B) {
+    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    float m = -INFINITY, s = 0.0f;
+    for (int64_t g = 0; g < G; ++g) {
+        const float2 p = ms[g * B + b];
+        ms_merge(m, s, p.x, p.y);
+    }
+    out[b] = ms_finalize(m, s, -INFINITY);
+}
+
+// gx = g[row] * exp(x - lse[row]) over chunks of one row.
+constexpr int kBwdUnroll = 4;
+
+__global__ void __launch_bounds__(kThreads) lse_bwd_kernel(
+    const float* __restrict__ g, const float* __restrict__ x,
+    const float* __restrict__ lse, float* __restrict__ gx, int64_t B, int64_t N,
+    int nchunk, int64_t chunk_vec) {
+    const int chunk = static_cast<int>(blockIdx.x % nchunk);
+    // rows are visited last-to-first: the forward pass streamed rows
+    // first-to-last, so the rows it read last are the likeliest still in L2
+    const int64_t row = B - 1 - static_cast<int64_t>(blockIdx.x / nchunk);
+    const float* xr = x + row * N;
+    float* gr = gx + row * N;
+    const float gs = __ldg(g + row);
+    const float ll = __ldg(lse + row) * kLog2e;
+    const int64_t head = head_elems(xr, N);
+    const int64_t nv = (N - head) / 4;
+    const int64_t tail0 = head + nv * 4;
+    const int64_t v0 = min(nv, chunk * chunk_vec), v1 = min(nv, v0 + chunk_vec);
+    const uint4* xv = reinterpret_cast<const uint4*>(xr + head);
+    float4* gv = reinterpret_cast<float4*>(gr + head);
+    auto op = [&](float v) { return gs * ex2(fmaf(v, kLog2e, -ll)); };
+    int64_t i = v0 + threadIdx.x;
+    for (; i + (kBwdUnroll - 1) * kThreads < v1; i += kBwdUnroll * kThreads) {
+        uint4 r[kBwdUnroll];
+#pragma unroll
+        for (int u = 0; u < kBwdUnroll; ++u) r[u] = ld_stream_u4(xv + i + u * kThreads);
+#pragma unroll
+        for (int u = 0; u < kBwdUnroll; ++u) {
+            float4 o = make_float4(op(__uint_as_float(r[u].x)), op(__uint_as_float(r[u].y)),
+                                   op(__uint_as_float(r[u].z)), op(__uint_as_float(r[u].w)));
+            st_stream_f4(gv + i + u * kThreads, o);
+        }
+    }
+    for (; i < v1; i += kThreads) {
+        const uint4 r = ld_stream_u4(xv + i);
+        float4 o = make_float4(op(__uint_as_float(r.x)), op(__uint_as_float(r.y)),
+                               op(__uint_as_float(r.z)), op(__uint_as_float(r.w)));
+        st_stream_f4(gv + i, o);
+    }
+    if (chunk == 0) {
+        if (threadIdx.x < head) gr[threadIdx.x] = op(__ldg(xr + threadIdx.x));
+        if (tail0 + threadIdx.x < N) gr[tail0 + threadIdx.x] = op(__ldg(xr + tail0 + threadIdx.x));
+    }
+}
+
+// Element-wise backward for x / gx buffers whose 16-byte phases differ.
+__global__ void lse_bwd_scalar_kernel(const float* __restrict__ g, const float* __restrict__ x,
+                                      const float* __restrict__ lse, float* __restrict__ gx,
+                                      int64_t B, int64_t N) {
+    const int64_t row = blockIdx.y;
+    const float gs = __ldg(g + row);
+    const float ll = __ldg(lse + row) * kLog2e;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < N;
+         i += (int64_t)gridDim.x * blockDim.x)
+        gx[row * N + i] = gs * ex2(fmaf(__ldg(x + row * N + i), kLog2e, -ll));
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+int env_int(const char* name, int dflt) {
+    const char* v = std::getenv(name);
+    if (!v || !*v) return dflt;
+    return std::atoi(v);
+}
+
+// Rows of at most this many bytes go one warp per row.
+constexpr int64_t kWarpRowBytes = 16 * 1024;
+
+template <typename T>
+int choose_nseg(int64_t B, int64_t N) {
+    static const int forced = env_int("FUSELSE_B200_NSEG", 0);
+    if (forced > 0) return forced < kMaxSeg ? forced : kMaxSeg;
+    const int64_t nv = N * (int64_t)sizeof(T) / 16;
+    // enough CTAs for ~4 resident per SM, but segments of >= 64 KB
+    const int64_t target = 4LL * sm_count();
+    int64_t nseg = (target + B - 1) / B;
+    const int64_t max_by_size = nv / 4096;
+    if (nseg > max_by_size) nseg = max_by_size;
+    if (nseg < 1) nseg = 1;
+    if (nseg > kMaxSeg) nseg = kMaxSeg;
+    return static_cast<int>(nseg);
+}
+
+template <typename T, bool PARTIAL>
+int launch_rows(const T* x, float* out, int64_t B, int64_t N, float empty_value,
+                cudaStream_t stream, const char* what) {
+    constexpr int U = sizeof(T) == 4 ? 4 : 2;
+    if (N * (int64_t)sizeof(T) <= kWarpRowBytes) {
+        const int64_t grid = (B + kWarps - 1) / kWarps;
+        FL_REQUIRE(grid <= INT32_MAX, "%s: B=%lld too large", what, (long long)B);
+        lse_warp_kernel<T, PARTIAL, U><<<(unsigned)grid, kThreads, 0, stream>>>(x, out, B, N, empty_value);
+        return check_launch(what);
+    }
+    const int nseg = choose_nseg<T>(B, N);
+    const int64_t grid = B * nseg;
+    FL_REQUIRE(grid <= INT32_MAX, "%s: B=%lld too large", what, (long long)B);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = nseg;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    FL_CUDA(cudaLaunchKernelEx(&cfg, lse_segment_kernel<T, PARTIAL, U>, x, out, B, N, nseg,
+                               empty_value));
+    return check_launch(what);
+}
+
+template <typename T>
+int check_rows(const void* x, const void* out, int64_t B, int64_t N, const char* what) {
+    FL_REQUIRE(B >= 0 && N >= 0, "%s: negative shape (%lld, %lld)", what, (long long)B, (long long)N);
+    FL_REQUIRE(B == 0 || out != nullptr, "%s: out is NULL", what);
+    FL_REQUIRE(B == 0 || N == 0 || x != nullptr, "%s: x is NULL", what);
+    FL_REQUIRE(aligned_to(x, sizeof(T)), "%s: x is not %d-byte aligned", what, (int)sizeof(T));
+    FL_REQUIRE(aligned_to(out, 4), "%s: out is not 4-byte aligned", what);
+    return FL_OK;
+}
+
+}  // namespace
+}  // namespace fl
+
+using namespace fl;
+
+extern "C" int fl_lse_f32_fwd(const float* x, float* out, int64_t B, int64_t N, int robust,
+                              fl_stream_t stream) {
+    clear_error();
+    if (int st = check_rows<float>(x, out, B, N, "fl_lse_f32_fwd")) return st;
+    if (B == 0) return FL_OK;
+    if (int st = bind_device(stream, out)) return st;
+    return launch_rows<float, false>(x, out, B, N, robust ? -INFINITY : -1.0e30f,
+                                     reinterpret_cast<cudaStream_t>(stream), "fl_lse_f32_fwd");
+}
+
+extern "C" int fl_lse_f16_fwd(const uint16_t* x, float* out, int64_t B, int64_t N,
+                              fl_stream_t stream) {
+    clear_error();
+    if (int st = check_rows<__half>(x, out, B, N, "fl_lse_f16_fwd")) return st;
+    if (B == 0) return FL_OK;
+    if (int st = bind_device(stream, out)) return st;
+    return launch_rows<__half, false>(reinterpret_cast<const __half*>(x), out, B, N, -1.0e30f,
+                                      reinterpret_cast<cudaStream_t>(stream), "fl_lse_f16_fwd");
+}
+
+extern "C" int fl_lse_f32_partial(const float* x, float* ms, int64_t B, int64_t N,
+                                  fl_stream_t stream) {
+    clear_error();
+    if (int st = check_rows<float>(x, ms, B, N, "fl_lse_f32_partial")) return st;
+    FL_REQUIRE(aligned_to(ms, 8), "fl_lse_f32_partial: ms is not 8-byte aligned");
+    if (B == 0) return FL_OK;
+    if (int st = bind_device(stream, ms)) return st;
+    return launch_rows<float, true>(x, ms, B, N, -INFINITY, reinterpret_cast<cudaStream_t>(stream),
+                                    "fl_lse_f32_partial");
+}
+
+extern "C" int fl_lse_f16_partial(const uint16_t* x, float* ms, int64_t B, int64_t N,
+                                  fl_stream_t stream) {
+    clear_error();
+    if (int st = check_rows<__half>(x, ms, B, N, "fl_lse_f16_partial")) return st;
+    FL_REQUIRE(aligned_to(ms, 8), "fl_lse_f16_partial: ms is not 8-byte aligned");
+    if (B == 0) return FL_OK;
+    if (int st = bind_device(stream, ms)) return st;
+    return launch_rows<__half, true>(reinterpret_cast<const __half*>(x), ms, B, N, -INFINITY,
+                                     reinterpret_cast<cudaStream_t>(stream), "fl_lse_f16_partial");
+}
+
+extern "C" int fl_lse_combine(const float* ms, float* out, int64_t G, int64_t B,
+                              fl_stream_t stream) {
+    clear_error();
+    FL_REQUIRE(G >= 0 && B >= 0, "fl_lse_combine: negative shape");
+    FL_REQUIRE(B == 0 || out != nullptr, "fl_lse_combine: out is NULL");
+    FL_REQUIRE(B == 0 || G == 0 || ms != nullptr, "fl_lse_combine: ms is NULL");
+    FL_REQUIRE(aligned_to(ms, 8) && aligned_to(out, 4), "fl_lse_combine: misaligned buffer");
+    if (B == 0) return FL_OK;
+    if (int st = bind_device(stream, out)) return st;
+    const int64_t grid = (B + 255) / 256;
+    FL_REQUIRE(grid <= INT32_MAX, "fl_lse_combine: B too large");
+    lse_combine_kernel<<<(unsigned)grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        reinterpret_cast<const float2*>(ms), out, G, B);
+    return check_launch("fl_lse_combine");
+}
+
+extern "C" int fl_lse_f32_bwd(const float* g, const float* x, const float* lse, float* gx,
+                              int64_t B, int64_t N, fl_stream_t stream) {
+    clear_error();
+    const char* what = "fl_lse_f32_bwd";
+    FL_REQUIRE(B >= 0 && N >= 0, "%s: negative shape", what);
+    if (B == 0 || N == 0) return FL_OK;
+    FL_REQUIRE(g && x && lse && gx, "%s: NULL buffer", what);
+    FL_REQUIRE(aligned_to(g, 4) && aligned_to(x, 4) && aligned_to(lse, 4) && aligned_to(gx, 4),
+               "%s: buffers must be 4-byte aligned", what);
+    if (int st = bind_device(stream, gx)) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const bool same_phase = ((reinterpret_cast<uintptr_t>(x) ^ reinterpret_cast<uintptr_t>(gx)) & 15u) == 0;
+    if (!same_phase) {
+        FL_REQUIRE(B <= 65535, "%s: B=%lld too large for buffers of differing alignment", what,
+                   (long long)B);
+        const int64_t bx = std::min<int64_t>((N + 255) / 256, 1024);
+        lse_bwd_scalar_kernel<<<dim3((unsigned)bx, (unsigned)B), 256, 0, s>>>(g, x, lse, gx, B, N);
+        return check_launch(what);
+    }
+    const int64_t nv = N / 4 + 1;
+    // ~64 KB of x per CTA
+    const int64_t chunk_vec = 4096;
+    const int64_t nchunk = (nv + chunk_vec - 1) / chunk_vec;
+    const int64_t grid = B * nchunk;
+    FL_REQUIRE(grid <= INT32_MAX, "%s: B*N too large", what);
+    lse_bwd_kernel<<<(unsigned)grid, kThreads, 0, s>>>(g, x, lse, gx, B, N, (int)nchunk, chunk_vec);
+    return check_launch(what);
+}

@@ -1,0 +1,256 @@
+"""Torch-facing entry points under the reference extension's method names.
+
+This module stands in for the `ext` object that the reference builds with
+`torch.utils.cpp_extension.load(...)` from each of its .cu files, so
+`make_fuselse_logsumexp(fuselse_b200.ext, robust)` and the experiment
+monkeypatches work unchanged.  Validation mirrors the reference TORCH_CHECKs
+(same conditions, RuntimeError), outputs are allocated with torch on the
+input's device, and kernels run on that device's current stream.
+
+Reference bindings replaced (file:line):
+  onepass_lse_float, onepass_lse_float_robust, onepass_lse_float_backward
+      fuselse/gpu/fused_fp32_kernel.cu:154-261
+  batched_logsumexp_fp16            fuselse/gpu/fused_fp16_kernel.cu:112-137
+  batched_logsumexp, batched_logsumexp_nolut
+                                    intlse/gpu/lse_kernel.cu:186-209
+  batched_logsumexp_q10_6           intlse/gpu/lse_kernel_q10_6.cu:144-170
+  sparse_forward_float              experiment_pyjuice/sparse_float_kernel.cu:110-172
+  sparse_forward_q16                experiment_pyjuice/sparse_q16_kernel.cu:139-207
+Additions without a reference counterpart: batched_logsumexp_q16_i32,
+lse_partial, lse_combine, sparse_log_weights.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import call, ptr
+
+
+def _check(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _stream(t: torch.Tensor):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+# --------------------------------------------------------------------------
+# FuseLSE fp32 (fused_fp32_kernel.cu)
+# --------------------------------------------------------------------------
+def _check_f32_2d(x: torch.Tensor) -> None:
+    _check(x.is_cuda, "x must be CUDA")
+    _check(x.dtype == torch.float32, "x must be float32")
+    _check(x.dim() == 2, "x must be 2D (B, N)")
+    _check(x.is_contiguous(), "x must be contiguous")
+
+
+def _lse_f32(x: torch.Tensor, robust: bool) -> torch.Tensor:
+    _check_f32_2d(x)
+    B, N = x.shape
+    out = torch.empty((B,), dtype=torch.float32, device=x.device)
+    if B == 0:
+        return out
+    call("fl_lse_f32_fwd", ptr(x), ptr(out), B, N, int(robust), _stream(x))
+    return out
+
+
+def onepass_lse_float(x: torch.Tensor) -> torch.Tensor:
+    """(B, N) fp32 -> (B,) fp32 log-sum-exp; finite inputs assumed."""
+    return _lse_f32(x, robust=False)
+
+
+def onepass_lse_float_robust(x: torch.Tensor) -> torch.Tensor:
+    """(B, N) fp32 -> (B,) fp32 log-sum-exp with IEEE NaN/Inf rules."""
+    return _lse_f32(x, robust=True)
+
+
+def onepass_lse_float_backward(grad_output: torch.Tensor, x: torch.Tensor,
+                               lse_output: torch.Tensor) -> torch.Tensor:
+    """grad_input = grad_output[:, None] * exp(x - lse_output[:, None])."""
+    _check(grad_output.is_cuda, "grad_output must be CUDA")
+    _check(x.is_cuda, "x must be CUDA")
+    _check(lse_output.is_cuda, "lse_output must be CUDA")
+    _check(x.dtype == torch.float32, "x must be float32")
+    _check(grad_output.dtype == torch.float32, "grad_output must be float32")
+    _check(lse_output.dtype == torch.float32, "lse_output must be float32")
+    _check(x.dim() == 2, "x must be 2D (B, N)")
+    _check(grad_output.dim() == 1, "grad_output must be 1D (B)")
+    _check(lse_output.dim() == 1, "lse_output must be 1D (B)")
+    _check(x.is_contiguous(), "x must be contiguous")
+    _check(grad_output.is_contiguous(), "grad_output must be contiguous")
+    _check(lse_output.is_contiguous(), "lse_output must be contiguous")
+    _check(grad_output.size(0) == x.size(0), "grad_output batch dimension must match x")
+    _check(lse_output.size(0) == x.size(0), "lse_output batch dimension must match x")
+    _check(grad_output.device == x.device and lse_output.device == x.device,
+           "grad_output, x and lse_output must be on the same device")
+    B, N = x.shape
+    grad_input = torch.empty_like(x)
+    if B * N == 0:
+        return grad_input
+    call("fl_lse_f32_bwd", ptr(grad_output), ptr(x), ptr(lse_output), ptr(grad_input), B, N,
+         _stream(x))
+    return grad_input
+
+
+# --------------------------------------------------------------------------
+# FuseLSE16 (fused_fp16_kernel.cu)
+# --------------------------------------------------------------------------
+def batched_logsumexp_fp16(input: torch.Tensor) -> torch.Tensor:
+    """(B, N) fp16 -> (B,) fp32 log-sum-exp, fp32 arithmetic."""
+    _check(input.dim() == 2, "Expected 2-D tensor (B, N)")
+    _check(input.is_cuda and input.dtype == torch.float16, "Input must be CUDA fp16")
+    _check(input.is_contiguous(), "Input must be contiguous")
+    B, N = input.shape
+    out = torch.empty((B,), dtype=torch.float32, device=input.device)
+    if B == 0:
+        return out
+    call("fl_lse_f16_fwd", ptr(input, ctypes.c_uint16), ptr(out), B, N, _stream(input))
+    return out
+
+
+# --------------------------------------------------------------------------
+# IntLSE (lse_kernel.cu, lse_kernel_q10_6.cu)
+# --------------------------------------------------------------------------
+def _check_intlse_f32(input: torch.Tensor) -> None:
+    _check(input.dim() == 2, "Expected 2-D tensor (B, N)")
+    _check(input.is_cuda and input.dtype == torch.float32,
+           "Expected input.is_cuda() && input.dtype() == torch::kFloat32 to be true, but got false.")
+    _check(input.is_contiguous(), "Input must be contiguous")
+
+
+def _intlse_f32(input: torch.Tensor, use_lut: bool) -> torch.Tensor:
+    _check_intlse_f32(input)
+    B, N = input.shape
+    out = torch.empty((B,), dtype=torch.float32, device=input.device)
+    if B == 0:
+        return out
+    call("fl_intlse_q16_f32", ptr(input), ptr(out), B, N, int(use_lut), _stream(input))
+    return out
+
+
+def batched_logsumexp(input: torch.Tensor) -> torch.Tensor:
+    """IntLSE Q16.16: (B, N) fp32 base-e -> (B,) fp32 base-e, bit-identical to the reference."""
+    return _intlse_f32(input, use_lut=True)
+
+
+def batched_logsumexp_nolut(input: torch.Tensor) -> torch.Tensor:
+    """IntLSE Q16.16 without the correction table (ablation)."""
+    return _intlse_f32(input, use_lut=False)
+
+
+def batched_logsumexp_q16_i32(input: torch.Tensor, use_lut: bool = True) -> torch.Tensor:
+    """IntLSE Q16.16 from int32 fixed-point input (base 2) -> (B,) fp32 base-e."""
+    _check(input.dim() == 2, "Expected 2-D tensor (B, N)")
+    _check(input.is_cuda, "Input must be CUDA")
+    _check(input.dtype == torch.int32, "Input must be int32 (Q16.16 base-2 fixed-point)")
+    _check(input.is_contiguous(), "Input must be contiguous")
+    B, N = input.shape
+    out = torch.empty((B,), dtype=torch.float32, device=input.device)
+    if B == 0:
+        return out
+    call("fl_intlse_q16_i32", ptr(input, ctypes.c_int32), ptr(out), B, N, int(use_lut),
+         _stream(input))
+    return out
+
+
+def batched_logsumexp_q10_6(input: torch.Tensor) -> torch.Tensor:
+    """IntLSE Q10.6: (B, N) int16 base-2 -> (B,) fp32 base-e, bit-identical to the reference."""
+    _check(input.dim() == 2, "Expected 2-D tensor (B, N)")
+    _check(input.is_cuda, "Input must be CUDA")
+    _check(input.dtype == torch.int16, "Input must be int16 (Q10.6 base-2 fixed-point)")
+    _check(input.is_contiguous(), "Input must be contiguous")
+    B, N = input.shape
+    out = torch.empty((B,), dtype=torch.float32, device=input.device)
+    if B == 0:
+        return out
+    call("fl_intlse_q10_6_i16", ptr(input, ctypes.c_int16), ptr(out), B, N, _stream(input))
+    return out
+
+
+# --------------------------------------------------------------------------
+# Vocab-shard partial states
+# --------------------------------------------------------------------------
+def lse_partial(x: torch.Tensor) -> torch.Tensor:
+    """(B, N) fp32/fp16 -> (B, 2) fp32 rows of (max, sum exp(x - max))."""
+    _check(x.dim() == 2, "Expected 2-D tensor (B, N)")
+    _check(x.is_cuda and x.dtype in (torch.float32, torch.float16), "Input must be CUDA fp32 or fp16")
+    _check(x.is_contiguous(), "Input must be contiguous")
+    B, N = x.shape
+    ms = torch.empty((B, 2), dtype=torch.float32, device=x.device)
+    if B == 0:
+        return ms
+    if x.dtype == torch.float32:
+        call("fl_lse_f32_partial", ptr(x), ptr(ms), B, N, _stream(x))
+    else:
+        call("fl_lse_f16_partial", ptr(x, ctypes.c_uint16), ptr(ms), B, N, _stream(x))
+    return ms
+
+
+def lse_combine(ms: torch.Tensor) -> torch.Tensor:
+    """(G, B, 2) shard partials -> (B,) fp32 log-sum-exp over all shards."""
+    _check(ms.dim() == 3 and ms.size(2) == 2, "Expected (G, B, 2) partial states")
+    _check(ms.is_cuda and ms.dtype == torch.float32, "Partials must be CUDA fp32")
+    _check(ms.is_contiguous(), "Partials must be contiguous")
+    G, B, _ = ms.shape
+    out = torch.empty((B,), dtype=torch.float32, device=ms.device)
+    if B == 0:
+        return out
+    call("fl_lse_combine", ptr(ms), ptr(out), G, B, _stream(ms))
+    return out
+
+
+# --------------------------------------------------------------------------
+# Sparse PC sum layer (sparse_float_kernel.cu / sparse_q16_kernel.cu)
+# --------------------------------------------------------------------------
+def _sparse(fn: str, node_mars, element_mars, params, nids, cids, pids, block_size: int,
+            err_flag=None) -> None:
+    _check(node_mars.is_cuda, "node_mars must be CUDA")
+    _check(element_mars.is_cuda, "element_mars must be CUDA")
+    _check(params.is_cuda, "params must be CUDA")
+    for name, t, dt in (("node_mars", node_mars, torch.float32),
+                        ("element_mars", element_mars, torch.float32),
+                        ("params", params, torch.float32),
+                        ("nids", nids, torch.int64), ("cids", cids, torch.int64),
+                        ("pids", pids, torch.int64)):
+        _check(t.dtype == dt, f"{name} must be {dt}")
+        _check(t.is_contiguous(), f"{name} must be contiguous")
+        _check(t.device == node_mars.device, f"{name} must be on {node_mars.device}")
+    _check(node_mars.dim() == 2 and element_mars.dim() == 2, "node_mars / element_mars must be 2-D")
+    _check(cids.dim() == 2 and pids.shape == cids.shape and nids.dim() == 1 and
+           nids.size(0) == cids.size(0), "nids (K,), cids and pids (K, E) expected")
+    batch = node_mars.size(1)
+    _check(element_mars.size(1) == batch, "element_mars and node_mars batch sizes differ")
+    num_nblocks, num_edges = cids.shape
+    ef = ptr(err_flag, ctypes.c_int) if err_flag is not None else None
+    call(fn, ptr(node_mars), ptr(element_mars), ptr(params), ptr(nids, ctypes.c_int64),
+         ptr(cids, ctypes.c_int64), ptr(pids, ctypes.c_int64), node_mars.size(0),
+         element_mars.size(0), params.numel(), num_nblocks, num_edges, batch, int(block_size),
+         ef, _stream(node_mars))
+
+
+def sparse_forward_float(node_mars, element_mars, params, nids, cids, pids, block_size) -> None:
+    """In place: node_mars[nids[k]+p, b] = LSE_e(log params[pids[k,e]+p] + element_mars[cids[k,e], b])."""
+    _sparse("fl_sparse_f32", node_mars, element_mars, params, nids, cids, pids, block_size)
+
+
+def sparse_forward_q16(node_mars, element_mars, params, nids, cids, pids, block_size) -> None:
+    """Q16.16 version of sparse_forward_float, bit-identical to the reference kernel."""
+    _sparse("fl_sparse_q16", node_mars, element_mars, params, nids, cids, pids, block_size)
+
+
+def sparse_log_weights(params: torch.Tensor) -> torch.Tensor:
+    """The device-formed log-weights __logf(fmaxf(w, 1e-45f)) the sparse kernels use."""
+    _check(params.is_cuda and params.dtype == torch.float32 and params.is_contiguous(),
+           "params must be contiguous CUDA fp32")
+    out = torch.empty_like(params)
+    if params.numel():
+        call("fl_sparse_log_weights", ptr(params), ptr(out), params.numel(), _stream(params))
+    return out
+
+
+def version() -> int:
+    return _lib.lib().fl_version()

@@ -1,0 +1,164 @@
+/*
+ * fuselse_b200 — C ABI of the B200 (sm_100a) row log-sum-exp library.
+ *
+ * Every entry point takes plain device pointers, int64 sizes and a CUDA
+ * stream, launches its kernels asynchronously on that stream and returns a
+ * status code (FL_OK == 0).  Nothing here allocates device memory: outputs
+ * are caller-owned buffers.  On a non-zero status, fl_last_error() returns a
+ * message for the calling thread.
+ *
+ * Pointer rules shared by all entry points:
+ *   - all pointers are device (or managed) memory of the device that owns
+ *     `stream` (the NULL stream means the device that owns the first input);
+ *   - arrays are dense row-major (C-contiguous), element-aligned;
+ *   - a NULL pointer is accepted only when the array it stands for is empty.
+ *
+ * Each function names the reference interface it replaces (file:line in the
+ * FuseLSE/IntLSE reference sources).
+ */
+#ifndef FUSELSE_B200_H
+#define FUSELSE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t, declared without pulling in CUDA headers. */
+typedef struct CUstream_st* fl_stream_t;
+
+enum fl_status {
+    FL_OK = 0,
+    FL_ERR_INVALID_ARGUMENT = 1, /* shape, pointer or alignment rejected */
+    FL_ERR_CUDA = 2,             /* a CUDA runtime call or launch failed */
+    FL_ERR_UNSUPPORTED = 3       /* well-formed request outside the supported range */
+};
+
+/* Message of the last failed call on this host thread ("" if none). */
+const char* fl_last_error(void);
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+int fl_version(void);
+
+/* ------------------------------------------------------------------------
+ * FuseLSE fp32 forward: out[b] = log(sum_n exp(x[b, n])), x (B, N) fp32.
+ *   robust != 0: IEEE rules — any NaN in the row -> NaN, else any +inf ->
+ *   +inf, -inf entries contribute nothing, an all--inf row -> -inf.
+ *   robust == 0: finite inputs assumed; an empty row (N == 0) gives -1e30.
+ * Replaces onepass_lse_float / onepass_lse_float_robust
+ * (fuselse/gpu/fused_fp32_kernel.cu:154-194, binding :255-259).
+ * ---------------------------------------------------------------------- */
+int fl_lse_f32_fwd(const float* x, float* out, int64_t B, int64_t N,
+                   int robust, fl_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * FuseLSE fp32 backward: gx[b, n] = g[b] * exp(x[b, n] - lse[b]).
+ * g, lse (B,), x and gx (B, N) fp32.
+ * Replaces onepass_lse_float_backward (fuselse/gpu/fused_fp32_kernel.cu:196-252).
+ * ---------------------------------------------------------------------- */
+int fl_lse_f32_bwd(const float* g, const float* x, const float* lse,
+                   float* gx, int64_t B, int64_t N, fl_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * FuseLSE16 forward: out[b] (fp32) = LSE over x[b, :] given as IEEE fp16
+ * (uint16 bit patterns), fp32 arithmetic.  Same rules as robust fp32.
+ * Replaces batched_logsumexp_fp16 (fuselse/gpu/fused_fp16_kernel.cu:112-132).
+ * ---------------------------------------------------------------------- */
+int fl_lse_f16_fwd(const uint16_t* x, float* out, int64_t B, int64_t N,
+                   fl_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Per-row partial state for vocab-sharded rows (no reference counterpart;
+ * it splits the reference's one-block-per-row reduction at a shard edge):
+ *   ms[2*b]   = m_b = max_n x[b, n]   (NaN if any NaN)
+ *   ms[2*b+1] = s_b = sum_n exp(x[b, n] - m'_b),  m'_b = (m_b == -inf ? 0 : m_b)
+ * `ms` holds B float pairs.  fp32 and fp16 inputs.
+ * ---------------------------------------------------------------------- */
+int fl_lse_f32_partial(const float* x, float* ms, int64_t B, int64_t N,
+                       fl_stream_t stream);
+int fl_lse_f16_partial(const uint16_t* x, float* ms, int64_t B, int64_t N,
+                       fl_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Combine G shard partials per row: ms (G, B, 2) as written by
+ * fl_lse_*_partial on each shard (shard-major), out (B,) fp32:
+ *   out[b] = M + log(sum_g s_gb * exp(m_gb - M)),  M = max_g m_gb
+ * with the robust rules (NaN wins, then +inf, all--inf gives -inf).
+ * ---------------------------------------------------------------------- */
+int fl_lse_combine(const float* ms, float* out, int64_t G, int64_t B,
+                   fl_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * IntLSE Q16.16 with fp32 base-e input: q = rint_sat(x * log2(e) * 2^16),
+ * pairwise base-2 Mitchell reduction with the 64-entry correction table
+ * (use_lut != 0) or without it (use_lut == 0), out = acc * ln2 / 2^16.
+ * Bit-identical to the reference kernel on the same input buffer.
+ * Replaces batched_logsumexp / batched_logsumexp_nolut
+ * (intlse/gpu/lse_kernel.cu:164-202, binding :204-209).
+ * ---------------------------------------------------------------------- */
+int fl_intlse_q16_f32(const float* x, float* out, int64_t B, int64_t N,
+                      int use_lut, fl_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * IntLSE Q16.16 with int32 input already in Q16.16 base-2 fixed point.
+ * Same reduction order as fl_intlse_q16_f32 minus the float conversion, so
+ * feeding q[b, n] = rint_sat(x[b, n] * log2(e) * 2^16) reproduces
+ * fl_intlse_q16_f32(x) (and the reference batched_logsumexp) bit for bit.
+ * Derived from intlse/gpu/lse_kernel.cu:67-159 (the conversion at :114 removed).
+ * ---------------------------------------------------------------------- */
+int fl_intlse_q16_i32(const int32_t* q, float* out, int64_t B, int64_t N,
+                      int use_lut, fl_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * IntLSE Q10.6: int16 (B, N) base-2 Q10.6 input -> fp32 base-e (B,).
+ * Bit-identical to the reference kernel.
+ * Replaces batched_logsumexp_q10_6 (intlse/gpu/lse_kernel_q10_6.cu:144-165).
+ * ---------------------------------------------------------------------- */
+int fl_intlse_q10_6_i16(const int16_t* q, float* out, int64_t B, int64_t N,
+                        fl_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Sparse probabilistic-circuit sum layer (pyjuice layout), in place:
+ *   for k in [0, num_nblocks), p in [0, block_size), b in [0, batch):
+ *     node_mars[(nids[k] + p) * batch + b] =
+ *         LSE_e( log(max(params[pids[k, e] + p], 1e-45)) + element_mars[cids[k, e] * batch + b] )
+ * node_mars (num_nodes, batch), element_mars (num_elements, batch), params
+ * (num_params,) fp32; nids (num_nblocks,), cids and pids (num_nblocks,
+ * num_edges) int64.  Index arrays are bounds-checked on the device: an
+ * out-of-range child or parameter index makes that output NaN, an
+ * out-of-range node index skips the write, and either sets *err_flag = 1
+ * when err_flag is non-NULL (a device int the caller zeroes first).
+ * fl_sparse_f32 replaces sparse_forward_float
+ * (experiment_pyjuice/sparse_float_kernel.cu:110-167);
+ * fl_sparse_q16 replaces sparse_forward_q16
+ * (experiment_pyjuice/sparse_q16_kernel.cu:139-202) and is bit-identical to it.
+ * ---------------------------------------------------------------------- */
+int fl_sparse_f32(float* node_mars, const float* element_mars,
+                  const float* params, const int64_t* nids,
+                  const int64_t* cids, const int64_t* pids,
+                  int64_t num_nodes, int64_t num_elements, int64_t num_params,
+                  int64_t num_nblocks, int64_t num_edges, int64_t batch,
+                  int64_t block_size, int* err_flag, fl_stream_t stream);
+int fl_sparse_q16(float* node_mars, const float* element_mars,
+                  const float* params, const int64_t* nids,
+                  const int64_t* cids, const int64_t* pids,
+                  int64_t num_nodes, int64_t num_elements, int64_t num_params,
+                  int64_t num_nblocks, int64_t num_edges, int64_t batch,
+                  int64_t block_size, int* err_flag, fl_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * The per-edge log-weight exactly as both sparse kernels form it on the
+ * device: logw[i] = __logf(fmaxf(params[i], 1e-45f)), n values.
+ * (experiment_pyjuice/sparse_q16_kernel.cu:102 and
+ * sparse_float_kernel.cu:76 compute the same expression in shared memory.)  Exposed so a host checker can replay the
+ * Q16.16 reduction bit for bit from device-formed log-weights.
+ * ---------------------------------------------------------------------- */
+int fl_sparse_log_weights(const float* params, float* logw, int64_t n,
+                          fl_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FUSELSE_B200_H */

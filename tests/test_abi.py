@@ -1,0 +1,65 @@
+"""CPU checks of the C-ABI boundary: the library loads and exports exactly what
+include/fuselse_b200.h declares (no compute calls without a GPU)."""
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "fuselse_b200.h"
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(?:int|const char\*)\s+(fl_\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    for must in ("fl_lse_f32_fwd", "fl_lse_f32_bwd", "fl_lse_f16_fwd", "fl_intlse_q16_f32",
+                 "fl_intlse_q16_i32", "fl_intlse_q10_6_i16", "fl_sparse_f32", "fl_sparse_q16",
+                 "fl_lse_combine", "fl_last_error"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    from fuselse_b200 import _lib
+    L = _lib.lib()
+    for name in declared_functions():
+        assert hasattr(L, name), f"{name} not exported"
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)],
+                         capture_output=True, text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (fl_\w+)", out))
+    assert exported == set(declared_functions())
+
+
+def test_binding_covers_header():
+    from fuselse_b200 import _lib
+    assert set(_lib.exported_symbols()) == set(declared_functions())
+
+
+def test_version_and_error_without_gpu():
+    from fuselse_b200 import _lib
+    L = _lib.lib()
+    assert L.fl_version() >= 100
+    # argument validation happens before any CUDA call
+    st = L.fl_lse_f32_fwd(None, None, -1, 5, 1, None)
+    assert st == _lib.FL_ERR_INVALID_ARGUMENT
+    assert b"negative" in L.fl_last_error()
+    st = L.fl_intlse_q16_f32(ctypes.cast(ctypes.c_void_p(2), ctypes.POINTER(ctypes.c_float)),
+                             ctypes.cast(ctypes.c_void_p(16), ctypes.POINTER(ctypes.c_float)),
+                             1, 4, 1, None)
+    assert st == _lib.FL_ERR_INVALID_ARGUMENT  # misaligned x
+    assert _lib.lib().fl_lse_f32_fwd(None, None, 0, 0, 1, None) == _lib.FL_OK  # empty is a no-op
+
+
+def test_library_is_sm100a_only():
+    from fuselse_b200 import _lib
+    r = subprocess.run(["cuobjdump", "--list-elf", str(_lib.LIB_PATH)], capture_output=True, text=True)
+    if r.returncode != 0:
+        pytest.skip("cuobjdump unavailable")
+    arches = set(re.findall(r"sm_(\d+a?)", r.stdout))
+    assert arches == {"100a"}, arches

@@ -1,0 +1,87 @@
+"""CPU tests of the host layer: validation and error behaviour of the
+reference-named entry points, the torch.logsumexp delegation rules of
+make_fuselse_logsumexp, and the partitioning helpers."""
+import pytest
+import torch
+
+import fuselse_b200
+from fuselse_b200 import distributed as D
+from fuselse_b200 import ext
+
+
+def test_ext_exposes_reference_names():
+    for name in ("onepass_lse_float", "onepass_lse_float_robust", "onepass_lse_float_backward",
+                 "batched_logsumexp_fp16", "batched_logsumexp", "batched_logsumexp_nolut",
+                 "batched_logsumexp_q10_6", "sparse_forward_float", "sparse_forward_q16"):
+        assert callable(getattr(ext, name))
+
+
+@pytest.mark.parametrize("fn,x,msg", [
+    (ext.onepass_lse_float, torch.zeros(2, 3), "x must be CUDA"),
+    (ext.onepass_lse_float_robust, torch.zeros(2, 3), "x must be CUDA"),
+    (ext.batched_logsumexp_fp16, torch.zeros(2, 3), "Input must be CUDA fp16"),
+    (ext.batched_logsumexp_fp16, torch.zeros(3), "Expected 2-D tensor (B, N)"),
+    (ext.batched_logsumexp, torch.zeros(2, 3), "Expected input.is_cuda()"),
+    (ext.batched_logsumexp_q10_6, torch.zeros(2, 3, dtype=torch.int16), "Input must be CUDA"),
+    (ext.batched_logsumexp_q16_i32, torch.zeros(2, 3, dtype=torch.int32), "Input must be CUDA"),
+])
+def test_validation_matches_reference_checks(fn, x, msg):
+    with pytest.raises(RuntimeError, match=msg.replace("(", r"\(").replace(")", r"\)")):
+        fn(x)
+
+
+def test_backward_validation():
+    with pytest.raises(RuntimeError, match="grad_output must be CUDA"):
+        ext.onepass_lse_float_backward(torch.zeros(2), torch.zeros(2, 3), torch.zeros(2))
+
+
+def test_sparse_validation():
+    z = torch.zeros(2, 2)
+    with pytest.raises(RuntimeError, match="node_mars must be CUDA"):
+        ext.sparse_forward_q16(z, z, torch.zeros(4), torch.zeros(1, dtype=torch.long),
+                               torch.zeros(1, 2, dtype=torch.long), torch.zeros(1, 2, dtype=torch.long), 1)
+
+
+def test_logsumexp_delegates_unsupported_inputs_to_torch():
+    lse = fuselse_b200.make_fuselse_logsumexp(ext, robust=True)
+    x = torch.randn(4, 7, 5, dtype=torch.float64)
+    torch.testing.assert_close(lse(x, dim=-1), torch.logsumexp(x, dim=-1))       # CPU
+    xf = x.float()
+    torch.testing.assert_close(lse(xf, dim=1, keepdim=True), torch.logsumexp(xf, dim=1, keepdim=True))
+    torch.testing.assert_close(lse(xf[..., :1], dim=-1), torch.logsumexp(xf[..., :1], dim=-1))
+    g = xf.clone().requires_grad_()
+    lse(g, dim=-1).sum().backward()
+    torch.testing.assert_close(g.grad, torch.softmax(xf, -1))
+
+
+def test_logsumexp_accepts_reference_style_extension_object():
+    calls = []
+
+    class Fake:
+        @staticmethod
+        def onepass_lse_float(x):
+            calls.append("plain")
+            return x.sum(-1)
+
+        onepass_lse_float_robust = onepass_lse_float
+        onepass_lse_float_backward = None
+
+    lse = fuselse_b200.make_fuselse_logsumexp(Fake, robust=False)
+    # CPU input is delegated, the fake is never called
+    lse(torch.zeros(2, 3))
+    assert calls == []
+
+
+@pytest.mark.parametrize("n,parts", [(10, 3), (512, 8), (7, 8), (0, 2), (128256, 8)])
+def test_split_range_partitions(n, parts):
+    blocks = [D.split_range(n, parts, i) for i in range(parts)]
+    assert blocks[0][0] == 0 and blocks[-1][1] == n
+    for (a, b), (c, d) in zip(blocks, blocks[1:]):
+        assert b == c and b >= a
+    sizes = [b - a for a, b in blocks]
+    assert max(sizes) - min(sizes) <= 1
+
+
+def test_split_range_rejects_bad_index():
+    with pytest.raises(ValueError):
+        D.split_range(10, 2, 2)
