@@ -16,7 +16,8 @@ Algorithmic bytes per step and GPU (the roofline numerator):
   backward 2*B*N*4 + 2*B*4            = 525,340,672 B  (read x, g, lse; write gx)
 Timing: W untimed warm-up steps; K timed steps, each bracketed by CUDA events
 on the launching stream (forward and backward separately), an L2 flush (a
-256 MiB write, > the 126 MB L2) between steps outside the events; barrier and
+256 MiB write, > the 126 MB L2, then a 256 MiB read that writes its dirty lines
+back) between steps outside the events; barrier and
 synchronize around the timed region; max over ranks.
 
 `--impl reference` times the reference's own CPU implementation of the path
@@ -145,7 +146,8 @@ class FwdBwdF32(Workload):
         self.lse = torch.empty(B, device=dev)
         self.config = {"workload": f"FuseLSE fp32 {'forward+backward' if do_bwd else 'forward'} "
                                    f"(B,N)=({B},{N}) per GPU, x~N(0,1), grad ones, robust",
-                       "B": B, "N": N, "l2": "flushed between steps (256 MiB write); input > L2",
+                       "B": B, "N": N,
+                       "l2": "flushed between steps (256 MiB write + 256 MiB read, untimed); input > L2",
                        "parallelism": "batch rows, one process per GPU, no collective"}
         self.launches_per_step = 2 if do_bwd else 1
 
@@ -297,8 +299,24 @@ def make_workload(name, dev, seed, world, rank):
 
 
 # ------------------------------------------------------------------ timing
+class L2Flush:
+    """Evicts L2 between timed steps: a 256 MiB write (> the 126 MB L2), then a
+    256 MiB read of another buffer so the write's dirty lines are written back
+    here, outside the timed events, instead of inside the next timed kernel."""
+
+    def __init__(self, dev):
+        n = 256 * 1024 * 1024 // 4
+        self.w = torch.empty(n, dtype=torch.float32, device=dev)
+        self.r = torch.ones(n, dtype=torch.float32, device=dev)
+        self.sink = torch.empty((), dtype=torch.float32, device=dev)
+
+    def __call__(self):
+        self.w.zero_()
+        torch.sum(self.r, dim=0, out=self.sink)
+
+
 def run_timed(wl, steps, warmup, dev, dist_on):
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    flush = L2Flush(dev)
     ks = wl.kernels()
     for _ in range(warmup):
         for _, fn, _ in ks:
@@ -309,7 +327,7 @@ def run_timed(wl, steps, warmup, dev, dist_on):
         torch.distributed.barrier()
     torch.cuda.synchronize()
     for k in range(steps):
-        flush.zero_()
+        flush()
         evs[k][0].record()
         for i, (_, fn, _) in enumerate(ks):
             fn()

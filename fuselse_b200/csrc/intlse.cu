@@ -31,6 +31,10 @@ namespace {
 
 enum Kind { kQ16F32 = 0, kQ16I32 = 1, kQ106I16 = 2 };
 
+#ifndef FL_INTLSE_DLONG
+#define FL_INTLSE_DLONG 32
+#endif
+
 // Reference constants (lse_kernel.cu:23-27): CONV = LOG2_E * 2^16 and
 // LN_2 / 2^16 from the same decimal literals, so the float values match.
 constexpr float kRefLog2e = 1.44269504089f;
@@ -117,7 +121,10 @@ __global__ void __launch_bounds__(CTA) intlse_rows_kernel(
     using In = typename IK<KIND>::In;
     constexpr int F = IK<KIND>::F;
     constexpr int C = 256 / CTA;
-    __shared__ int lut_s[64 * 32];
+    // long chains (D > 4) take the warp-uniform table skip; short ones need the
+    // table too often for the vote to pay
+    constexpr bool kSkip = D > 4;
+    __shared__ __align__(16) int lut_s[64 * 32];
     __shared__ int warp_val[8];
 
     const int rank = C > 1 ? static_cast<int>(blockIdx.x % C) : 0;
@@ -126,8 +133,7 @@ __global__ void __launch_bounds__(CTA) intlse_rows_kernel(
     const int t = rank * CTA + threadIdx.x;
 
     if constexpr (LUT) {
-        const int* src = F == 16 ? kLutQ16 : kLutQ10_6;
-        for (int i = threadIdx.x; i < 64 * 32; i += CTA) lut_s[i] = src[i >> 5];
+        fill_lane_lut<CTA>(lut_s, F == 16 ? kLutQ16 : kLutQ10_6);
         __syncthreads();
     }
     const LaneLut lut{lut_s + lane};
@@ -170,8 +176,13 @@ __global__ void __launch_bounds__(CTA) intlse_rows_kernel(
                     const int64_t in = (k + D) * 256 + t;
                     if (k + D < K && in < nv) buf[d] = load_vec<KIND>(vbase, in);
                     const bool active = k * 256 + t < nv;
+                    if constexpr (kSkip) {
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) pair_warp<F, LUT>(acc, cur.v[e], active, lut);
+                        for (int e = 0; e < 4; ++e) pair_warp<F, LUT>(acc, cur.v[e], active, lut);
+                    } else if (active) {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) acc = pair_exact<F, LUT>(acc, cur.v[e], lut);
+                    }
                 }
             }
         }
@@ -257,8 +268,11 @@ int launch_intlse(const typename IK<KIND>::In* x, float* out, int64_t B, int64_t
     FL_REQUIRE(B * C <= (int64_t)INT32_MAX, "%s: B=%lld too large", what, (long long)B);
     const int64_t K = (N / 4 + 255) / 256;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    int st = K > 8 ? launch_d<KIND, LUT, 16>(x, out, B, N, C, s)
-                   : launch_d<KIND, LUT, 4>(x, out, B, N, C, s);
+    // vectors each chain keeps in flight: deeper for long rows, whose few chains
+    // must cover the whole memory latency by themselves
+    int st = K > 64  ? launch_d<KIND, LUT, FL_INTLSE_DLONG>(x, out, B, N, C, s)
+             : K > 8 ? launch_d<KIND, LUT, 16>(x, out, B, N, C, s)
+                     : launch_d<KIND, LUT, 4>(x, out, B, N, C, s);
     if (st) return st;
     return check_launch(what);
 }

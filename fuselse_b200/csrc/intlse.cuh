@@ -52,6 +52,15 @@ struct LaneLut {
     __device__ __forceinline__ int operator[](uint32_t i) const { return base[i * 32]; }
 };
 
+// Fills the 64 x 32-word replicated table (16-byte aligned) with 16-byte stores.
+template <int THREADS>
+__device__ __forceinline__ void fill_lane_lut(int* dst, const int* src) {
+    for (int i = threadIdx.x; i < 64 * 32 / 4; i += THREADS) {
+        const int v = src[i >> 3];
+        reinterpret_cast<int4*>(dst)[i] = make_int4(v, v, v, v);
+    }
+}
+
 template <int F>
 __device__ __forceinline__ uint32_t lut_index(uint32_t M) {
     if constexpr (F == 16) {

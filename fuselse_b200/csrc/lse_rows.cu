@@ -28,6 +28,22 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
+
+// Forward segment kernel shape: threads per CTA, 16-byte vectors in flight per
+// thread (fp32 / fp16), software pipelining of the vector loop.
+#ifndef FL_FWD_THREADS
+#define FL_FWD_THREADS 256
+#endif
+#ifndef FL_FWD_U32
+#define FL_FWD_U32 4
+#endif
+#ifndef FL_FWD_U16
+#define FL_FWD_U16 2
+#endif
+#ifndef FL_FWD_PIPE
+#define FL_FWD_PIPE 0
+#endif
+constexpr int kFwdThreads = FL_FWD_THREADS;
 constexpr int kMaxSeg = 8;  // portable cluster size
 
 // Element traits: how many elements one 16-byte vector carries and how to
@@ -107,6 +123,30 @@ __device__ __forceinline__ void fold_vectors(const T* vbase, int64_t v0, int64_t
     constexpr int E = Elem<T>::kPerVec;
     const uint4* vp = reinterpret_cast<const uint4*>(vbase);
     int64_t i = v0 + first;
+#if FL_FWD_PIPE
+    // software pipeline: the next U vectors are in flight while this group folds
+    const int64_t step = (int64_t)U * stride;
+    if (i + (int64_t)(U - 1) * stride < v1) {
+        uint4 cur[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) cur[u] = ld_stream_u4(vp + i + (int64_t)u * stride);
+        for (i += step; i + (int64_t)(U - 1) * stride < v1; i += step) {
+            uint4 nxt[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) nxt[u] = ld_stream_u4(vp + i + (int64_t)u * stride);
+            float v[U * E];
+#pragma unroll
+            for (int u = 0; u < U; ++u) Elem<T>::unpack(cur[u], v + u * E);
+            ms_fold<U * E>(m, s, v);
+#pragma unroll
+            for (int u = 0; u < U; ++u) cur[u] = nxt[u];
+        }
+        float v[U * E];
+#pragma unroll
+        for (int u = 0; u < U; ++u) Elem<T>::unpack(cur[u], v + u * E);
+        ms_fold<U * E>(m, s, v);
+    }
+#endif
     for (; i + (int64_t)(U - 1) * stride < v1; i += (int64_t)U * stride) {
         uint4 r[U];
 #pragma unroll
@@ -124,7 +164,9 @@ __device__ __forceinline__ void fold_vectors(const T* vbase, int64_t v0, int64_t
 }
 
 // Block-wide merge; the result is valid in thread 0.
+template <int THREADS>
 __device__ __forceinline__ void ms_block_reduce(float& m, float& s) {
+    constexpr int kWarps = THREADS / 32;
     __shared__ float2 part[kWarps];
     ms_warp_allreduce(m, s);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -146,7 +188,7 @@ __device__ __forceinline__ void ms_block_reduce(float& m, float& s) {
 // One CTA per row segment; the nseg CTAs of a row form one cluster.
 // PARTIAL: write (m, s) pairs instead of the finished value.
 template <typename T, bool PARTIAL, int U>
-__global__ void __launch_bounds__(kThreads) lse_segment_kernel(
+__global__ void __launch_bounds__(kFwdThreads) lse_segment_kernel(
     const T* __restrict__ x, float* __restrict__ out, int64_t B, int64_t N,
     int nseg, float empty_value) {
     constexpr int E = Elem<T>::kPerVec;
@@ -163,14 +205,14 @@ __global__ void __launch_bounds__(kThreads) lse_segment_kernel(
         const int64_t tail0 = head + nv * E;
         const int64_t per = (nv + nseg - 1) / nseg;
         const int64_t v0 = min(nv, per * rank), v1 = min(nv, v0 + per);
-        fold_vectors<T, U>(rowp + head, v0, v1, threadIdx.x, kThreads, m, s);
+        fold_vectors<T, U>(rowp + head, v0, v1, threadIdx.x, kFwdThreads, m, s);
         if (rank == 0) {
             // at most E-1 head and E-1 tail elements
             if (threadIdx.x < head) ms_fold1(m, s, Elem<T>::load1(rowp + threadIdx.x));
             if (tail0 + threadIdx.x < N) ms_fold1(m, s, Elem<T>::load1(rowp + tail0 + threadIdx.x));
         }
     }
-    ms_block_reduce(m, s);
+    ms_block_reduce<kFwdThreads>(m, s);
     if (nseg > 1) {
         if (threadIdx.x == 0) {
             float2* dst = cluster.map_shared_rank(seg_part, 0);
@@ -320,7 +362,7 @@ int choose_nseg(int64_t B, int64_t N) {
 template <typename T, bool PARTIAL>
 int launch_rows(const T* x, float* out, int64_t B, int64_t N, float empty_value,
                 cudaStream_t stream, const char* what) {
-    constexpr int U = sizeof(T) == 4 ? 4 : 2;
+    constexpr int U = sizeof(T) == 4 ? FL_FWD_U32 : FL_FWD_U16;
     if (N * (int64_t)sizeof(T) <= kWarpRowBytes) {
         const int64_t grid = (B + kWarps - 1) / kWarps;
         FL_REQUIRE(grid <= INT32_MAX, "%s: B=%lld too large", what, (long long)B);
@@ -332,7 +374,7 @@ int launch_rows(const T* x, float* out, int64_t B, int64_t N, float empty_value,
     FL_REQUIRE(grid <= INT32_MAX, "%s: B=%lld too large", what, (long long)B);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(kFwdThreads);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];

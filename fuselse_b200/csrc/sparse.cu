@@ -30,7 +30,12 @@ namespace fl {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kTileCols = 64;
+// Batch columns per tile: the tile's slice of element_mars (rows x cols x 4 B)
+// is what must stay L2-resident while every parent gathers from it.
+#ifndef FL_SPARSE_TILE
+#define FL_SPARSE_TILE 32
+#endif
+constexpr int kTileCols = FL_SPARSE_TILE;
 constexpr int kGroup = 8;                       // gathers in flight per thread
 constexpr int kMetaBudget = 96 * 1024;          // shared-memory bytes for staged edges
 constexpr float kConvQ16 = 1.44269504089f * 65536.0f;
@@ -153,7 +158,7 @@ __global__ void __launch_bounds__(kThreads) sparse_kernel(SparseArgs A) {
     constexpr int TPN = kTileCols / VEC;  // threads per node within a tile
     constexpr int NPP = kThreads / TPN;   // nodes per pass
     extern __shared__ __align__(16) unsigned char smem[];
-    __shared__ int lut_s[Q16 ? 64 * 32 : 1];
+    __shared__ __align__(16) int lut_s[Q16 ? 64 * 32 : 4];
 
     const int64_t n0 = (int64_t)blockIdx.x * A.nodes_per_cta;
     const int64_t n1 = min(A.num_out, n0 + A.nodes_per_cta);
@@ -165,9 +170,7 @@ __global__ void __launch_bounds__(kThreads) sparse_kernel(SparseArgs A) {
     long long* s_row = reinterpret_cast<long long*>(
         smem + (((size_t)nn * E * 8 + 15) & ~(size_t)15));  // output row, or -1 (skip), flag in bit 62
 
-    if constexpr (Q16) {
-        for (int i = threadIdx.x; i < 64 * 32; i += kThreads) lut_s[i] = kLutQ16[i >> 5];
-    }
+    if constexpr (Q16) fill_lane_lut<kThreads>(lut_s, kLutQ16);
     // stage edges of [n0, n1)
     for (int64_t i = threadIdx.x; i < (int64_t)nn * E; i += kThreads) {
         const int ln = static_cast<int>(i / E), e = static_cast<int>(i % E);
