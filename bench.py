@@ -15,9 +15,10 @@ Algorithmic bytes per step and GPU (the roofline numerator):
   forward  B*N*4 + B*4                = 262,670,336 B
   backward 2*B*N*4 + 2*B*4            = 525,340,672 B  (read x, g, lse; write gx)
 Timing: W untimed warm-up steps; K timed steps, each bracketed by CUDA events
-on the launching stream (forward and backward separately), an L2 flush (a
-256 MiB write, > the 126 MB L2, then a 256 MiB read that writes its dirty lines
-back) between steps outside the events; barrier and
+on the launching stream (forward and backward separately), steps back to back
+with inputs larger than L2 (x and gx are 262 MB each, L2 126 MB; each kernel
+pays the write-back of the previous kernel's dirty lines, as in a training
+loop); `--flush-l2` instead evicts L2 between steps outside the events; barrier and
 synchronize around the timed region; max over ranks.
 
 `--impl reference` times the reference's own CPU implementation of the path
@@ -147,7 +148,7 @@ class FwdBwdF32(Workload):
         self.config = {"workload": f"FuseLSE fp32 {'forward+backward' if do_bwd else 'forward'} "
                                    f"(B,N)=({B},{N}) per GPU, x~N(0,1), grad ones, robust",
                        "B": B, "N": N,
-                       "l2": "flushed between steps (256 MiB write + 256 MiB read, untimed); input > L2",
+                       "l2": "inputs larger than L2 (x 262 MB, gx 262 MB), steps back to back",
                        "parallelism": "batch rows, one process per GPU, no collective"}
         self.launches_per_step = 2 if do_bwd else 1
 
@@ -203,7 +204,7 @@ class F16Vocab(Workload):
         self.world = world
         self.config = {"workload": "FuseLSE16 vocab shard (8192,16032) fp16 of (8192,128256); "
                                    "partial (max,sumexp) + NCCL all-gather + combine",
-                       "l2": "flushed between steps; input > L2"}
+                       "l2": "inputs larger than L2, steps back to back"}
         self.launches_per_step = 2
 
     def _step(self):
@@ -233,7 +234,7 @@ class IntLSE(Workload):
         self.dtype = "int32" if kind == "q16" else "int16"
         self.B, self.N = B, N
         self.config = {"workload": f"IntLSE {kind} (B,N)=({B},{N}), x~N(0,2^2)",
-                       "l2": "flushed between steps; input > L2"}
+                       "l2": "inputs larger than L2, steps back to back"}
         self.launches_per_step = 1
 
     def _step(self):
@@ -262,7 +263,7 @@ class Sparse(Workload):
         self.bytes = P * batch * 4 + S * batch * 4 + S * E * (8 + 8 + 4) + S * 8
         self.S = S
         self.config = {"workload": f"sparse PC sum layer {'Q16.16' if q16 else 'fp32'}: P={P}, S={S}, "
-                                   f"E={E}, batch={batch}", "l2": "flushed between steps"}
+                                   f"E={E}, batch={batch}", "l2": "inputs larger than L2, steps back to back"}
         self.launches_per_step = 1
 
     def _step(self):
@@ -315,8 +316,10 @@ class L2Flush:
         torch.sum(self.r, dim=0, out=self.sink)
 
 
-def run_timed(wl, steps, warmup, dev, dist_on):
-    flush = L2Flush(dev)
+def run_timed(wl, steps, warmup, dev, dist_on, flush_l2=False):
+    """Steps back to back (inputs larger than L2), or with an untimed L2Flush
+    between steps; CUDA events around every kernel."""
+    flush = L2Flush(dev) if flush_l2 else (lambda: None)
     ks = wl.kernels()
     for _ in range(warmup):
         for _, fn, _ in ks:
@@ -460,6 +463,7 @@ def main():
     ap.add_argument("--workload", default="fwdbwd_f32")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--flush-l2", action="store_true", help="evict L2 between timed steps")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -479,7 +483,7 @@ def main():
 
     wl = make_workload(args.workload, dev, seed=rank, world=world, rank=rank)
     with ClockSampler(local) as clk:
-        step_ms, per_kernel = run_timed(wl, args.steps, args.warmup, dev, dist_on)
+        step_ms, per_kernel = run_timed(wl, args.steps, args.warmup, dev, dist_on, args.flush_l2)
     clocks = clk.summary()
     step_ms = max_over_ranks(step_ms, dist_on, dev)
     per_kernel = [max_over_ranks(v, dist_on, dev) for v in per_kernel]

@@ -19,10 +19,20 @@ void set_error(const char* fmt, ...) {
 
 void clear_error() { g_last_error.clear(); }
 
+// The device of the last stream seen on this thread.  Repeated calls on one
+// stream (the common case, and every call while that stream is being captured
+// into a CUDA graph) make no device query.
+static thread_local fl_stream_t t_last_stream = nullptr;
+static thread_local int t_last_dev = -1;
+
 int bind_device(fl_stream_t stream, const void* ptr) {
     int dev = -1;
-    if (stream != nullptr) {
+    if (stream != nullptr && stream == t_last_stream) {
+        dev = t_last_dev;
+    } else if (stream != nullptr) {
         FL_CUDA(cudaStreamGetDevice(reinterpret_cast<cudaStream_t>(stream), &dev));
+        t_last_stream = stream;
+        t_last_dev = dev;
     } else if (ptr != nullptr) {
         cudaPointerAttributes attr;
         FL_CUDA(cudaPointerGetAttributes(&attr, ptr));

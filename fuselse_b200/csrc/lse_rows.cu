@@ -6,10 +6,11 @@
 //   * online (max, sum-exp) state per thread: one MUFU.EX2 per element instead
 //     of the reference's exp + log pair per element;
 //   * 16-byte streaming loads (ld.global.nc, no L1 allocation, 256 B L2
-//     prefetch), U vectors in flight per thread;
-//   * long rows are split into `nseg` contiguous segments, one CTA each, the
-//     CTAs of a row forming a thread-block cluster whose partial states are
-//     merged through distributed shared memory (no global scratch, one launch);
+//     prefetch), U vectors in flight per thread (FwdShape);
+//   * one CTA per row while rows are plentiful (B >= 2 x SMs); scarce long
+//     rows are split into `nseg` contiguous segments, one CTA each, the CTAs
+//     of a row forming a thread-block cluster whose partial states are merged
+//     through distributed shared memory (no global scratch, one launch);
 //   * short rows go one warp per row (8 rows per 256-thread CTA).
 // Backward (replaces logsumexp_float_backward_kernel, fused_fp32_kernel.cu:135-150):
 //   row-chunked grid (no per-element division), 16-byte load + 16-byte
@@ -29,22 +30,24 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 
-// Forward segment kernel shape: threads per CTA, 16-byte vectors in flight per
-// thread (fp32 / fp16), software pipelining of the vector loop.
-#ifndef FL_FWD_THREADS
-#define FL_FWD_THREADS 256
-#endif
-#ifndef FL_FWD_U32
-#define FL_FWD_U32 4
-#endif
-#ifndef FL_FWD_U16
-#define FL_FWD_U16 2
-#endif
-#ifndef FL_FWD_PIPE
-#define FL_FWD_PIPE 0
-#endif
-constexpr int kFwdThreads = FL_FWD_THREADS;
 constexpr int kMaxSeg = 8;  // portable cluster size
+
+// Forward segment-kernel shape per element type (measured on B200): threads per
+// CTA, 16-byte vectors per thread per group, and whether the next group's
+// loads are issued before the current group is folded.  fp16 carries twice
+// the elements per byte, so it keeps more bytes in flight per thread.
+template <typename T>
+struct FwdShape;
+template <>
+struct FwdShape<float> {
+    static constexpr int kThreads = 256, kU = 4;
+    static constexpr bool kPipe = false;
+};
+template <>
+struct FwdShape<__half> {
+    static constexpr int kThreads = 128, kU = 8;
+    static constexpr bool kPipe = true;
+};
 
 // Element traits: how many elements one 16-byte vector carries and how to
 // widen them to fp32.
@@ -117,16 +120,15 @@ __device__ __forceinline__ int64_t head_elems(const T* rowp, int64_t N) {
 
 // Accumulate vectors [v0, v1) of a row (vector i starts at element head + i*E)
 // with `stride` threads, this thread starting at `first`.
-template <typename T, int U>
+template <typename T, int U, bool PIPE>
 __device__ __forceinline__ void fold_vectors(const T* vbase, int64_t v0, int64_t v1,
                                              int first, int stride, float& m, float& s) {
     constexpr int E = Elem<T>::kPerVec;
     const uint4* vp = reinterpret_cast<const uint4*>(vbase);
     int64_t i = v0 + first;
-#if FL_FWD_PIPE
     // software pipeline: the next U vectors are in flight while this group folds
     const int64_t step = (int64_t)U * stride;
-    if (i + (int64_t)(U - 1) * stride < v1) {
+    if (PIPE && i + (int64_t)(U - 1) * stride < v1) {
         uint4 cur[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) cur[u] = ld_stream_u4(vp + i + (int64_t)u * stride);
@@ -146,8 +148,7 @@ __device__ __forceinline__ void fold_vectors(const T* vbase, int64_t v0, int64_t
         for (int u = 0; u < U; ++u) Elem<T>::unpack(cur[u], v + u * E);
         ms_fold<U * E>(m, s, v);
     }
-#endif
-    for (; i + (int64_t)(U - 1) * stride < v1; i += (int64_t)U * stride) {
+    for (; i + (int64_t)(U - 1) * stride < v1; i += step) {
         uint4 r[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) r[u] = ld_stream_u4(vp + i + (int64_t)u * stride);
@@ -187,8 +188,8 @@ __device__ __forceinline__ void ms_block_reduce(float& m, float& s) {
 
 // One CTA per row segment; the nseg CTAs of a row form one cluster.
 // PARTIAL: write (m, s) pairs instead of the finished value.
-template <typename T, bool PARTIAL, int U>
-__global__ void __launch_bounds__(kFwdThreads) lse_segment_kernel(
+template <typename T, bool PARTIAL>
+__global__ void __launch_bounds__(FwdShape<T>::kThreads) lse_segment_kernel(
     const T* __restrict__ x, float* __restrict__ out, int64_t B, int64_t N,
     int nseg, float empty_value) {
     constexpr int E = Elem<T>::kPerVec;
@@ -205,14 +206,15 @@ __global__ void __launch_bounds__(kFwdThreads) lse_segment_kernel(
         const int64_t tail0 = head + nv * E;
         const int64_t per = (nv + nseg - 1) / nseg;
         const int64_t v0 = min(nv, per * rank), v1 = min(nv, v0 + per);
-        fold_vectors<T, U>(rowp + head, v0, v1, threadIdx.x, kFwdThreads, m, s);
+        fold_vectors<T, FwdShape<T>::kU, FwdShape<T>::kPipe>(rowp + head, v0, v1, threadIdx.x,
+                                                              FwdShape<T>::kThreads, m, s);
         if (rank == 0) {
             // at most E-1 head and E-1 tail elements
             if (threadIdx.x < head) ms_fold1(m, s, Elem<T>::load1(rowp + threadIdx.x));
             if (tail0 + threadIdx.x < N) ms_fold1(m, s, Elem<T>::load1(rowp + tail0 + threadIdx.x));
         }
     }
-    ms_block_reduce<kFwdThreads>(m, s);
+    ms_block_reduce<FwdShape<T>::kThreads>(m, s);
     if (nseg > 1) {
         if (threadIdx.x == 0) {
             float2* dst = cluster.map_shared_rank(seg_part, 0);
@@ -236,7 +238,7 @@ __global__ void __launch_bounds__(kFwdThreads) lse_segment_kernel(
 }
 
 // One warp per row for short rows.
-template <typename T, bool PARTIAL, int U>
+template <typename T, bool PARTIAL>
 __global__ void __launch_bounds__(kThreads) lse_warp_kernel(
     const T* __restrict__ x, float* __restrict__ out, int64_t B, int64_t N,
     float empty_value) {
@@ -249,7 +251,7 @@ __global__ void __launch_bounds__(kThreads) lse_warp_kernel(
     const int64_t nv = (N - head) / E;
     const int64_t tail0 = head + nv * E;
     float m = -INFINITY, s = 0.0f;
-    fold_vectors<T, U>(rowp + head, 0, nv, lane, 32, m, s);
+    fold_vectors<T, FwdShape<T>::kU, false>(rowp + head, 0, nv, lane, 32, m, s);
     if (lane < head) ms_fold1(m, s, Elem<T>::load1(rowp + lane));
     if (tail0 + lane < N) ms_fold1(m, s, Elem<T>::load1(rowp + tail0 + lane));
     ms_warp_allreduce(m, s);
@@ -282,9 +284,7 @@ __global__ void __launch_bounds__(kThreads) lse_bwd_kernel(
     const float* __restrict__ lse, float* __restrict__ gx, int64_t B, int64_t N,
     int nchunk, int64_t chunk_vec) {
     const int chunk = static_cast<int>(blockIdx.x % nchunk);
-    // rows are visited last-to-first: the forward pass streamed rows
-    // first-to-last, so the rows it read last are the likeliest still in L2
-    const int64_t row = B - 1 - static_cast<int64_t>(blockIdx.x / nchunk);
+    const int64_t row = static_cast<int64_t>(blockIdx.x / nchunk);
     const float* xr = x + row * N;
     float* gr = gx + row * N;
     const float gs = __ldg(g + row);
@@ -349,10 +349,13 @@ int choose_nseg(int64_t B, int64_t N) {
     static const int forced = env_int("FUSELSE_B200_NSEG", 0);
     if (forced > 0) return forced < kMaxSeg ? forced : kMaxSeg;
     const int64_t nv = N * (int64_t)sizeof(T) / 16;
-    // enough CTAs for ~4 resident per SM, but segments of >= 64 KB
-    const int64_t target = 4LL * sm_count();
+    // One CTA per row is fastest whenever there are rows enough to fill the SMs
+    // (a cluster's CTAs wait on one another at the end, holding their slots);
+    // scarce rows are split up to 2 CTAs per SM, segments of >= 32 KB.
+    const int64_t target = 2LL * sm_count();
+    if (B >= target) return 1;
     int64_t nseg = (target + B - 1) / B;
-    const int64_t max_by_size = nv / 4096;
+    const int64_t max_by_size = nv / 2048;
     if (nseg > max_by_size) nseg = max_by_size;
     if (nseg < 1) nseg = 1;
     if (nseg > kMaxSeg) nseg = kMaxSeg;
@@ -362,11 +365,10 @@ int choose_nseg(int64_t B, int64_t N) {
 template <typename T, bool PARTIAL>
 int launch_rows(const T* x, float* out, int64_t B, int64_t N, float empty_value,
                 cudaStream_t stream, const char* what) {
-    constexpr int U = sizeof(T) == 4 ? FL_FWD_U32 : FL_FWD_U16;
     if (N * (int64_t)sizeof(T) <= kWarpRowBytes) {
         const int64_t grid = (B + kWarps - 1) / kWarps;
         FL_REQUIRE(grid <= INT32_MAX, "%s: B=%lld too large", what, (long long)B);
-        lse_warp_kernel<T, PARTIAL, U><<<(unsigned)grid, kThreads, 0, stream>>>(x, out, B, N, empty_value);
+        lse_warp_kernel<T, PARTIAL><<<(unsigned)grid, kThreads, 0, stream>>>(x, out, B, N, empty_value);
         return check_launch(what);
     }
     const int nseg = choose_nseg<T>(B, N);
@@ -374,7 +376,7 @@ int launch_rows(const T* x, float* out, int64_t B, int64_t N, float empty_value,
     FL_REQUIRE(grid <= INT32_MAX, "%s: B=%lld too large", what, (long long)B);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(kFwdThreads);
+    cfg.blockDim = dim3(FwdShape<T>::kThreads);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -384,7 +386,7 @@ int launch_rows(const T* x, float* out, int64_t B, int64_t N, float empty_value,
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    FL_CUDA(cudaLaunchKernelEx(&cfg, lse_segment_kernel<T, PARTIAL, U>, x, out, B, N, nseg,
+    FL_CUDA(cudaLaunchKernelEx(&cfg, lse_segment_kernel<T, PARTIAL>, x, out, B, N, nseg,
                                empty_value));
     return check_launch(what);
 }

@@ -31,9 +31,12 @@ namespace {
 
 constexpr int kThreads = 256;
 // Batch columns per tile: the tile's slice of element_mars (rows x cols x 4 B)
-// is what must stay L2-resident while every parent gathers from it.
+// is what L2 should hold while every parent gathers from it; wider tiles also
+// make each gathered child chunk longer (cols x 4 B contiguous), and on B200
+// the 256-byte chunks of 64-column tiles measured fastest (16: 1.31 ms,
+// 32: 0.70 ms, 64: 0.53 ms for the fp32 layer at P=262144, S=65536, E=32).
 #ifndef FL_SPARSE_TILE
-#define FL_SPARSE_TILE 32
+#define FL_SPARSE_TILE 64
 #endif
 constexpr int kTileCols = FL_SPARSE_TILE;
 constexpr int kGroup = 8;                       // gathers in flight per thread
