@@ -14,8 +14,10 @@ ranks / max-over-ranks device time.
 Algorithmic bytes per step and GPU (the roofline numerator):
   forward  B*N*4 + B*4                = 262,670,336 B
   backward 2*B*N*4 + 2*B*4            = 525,340,672 B  (read x, g, lse; write gx)
-Timing: W untimed warm-up steps; K timed steps, each bracketed by CUDA events
-on the launching stream (forward and backward separately), steps back to back
+Timing: W untimed warm-up steps; K timed steps, each kernel replayed from its
+own CUDA graph (captured once through the public entry points; `--eager` calls
+them directly) and bracketed by CUDA events on the launching stream (forward
+and backward separately), steps back to back
 with inputs larger than L2 (x and gx are 262 MB each, L2 126 MB; each kernel
 pays the write-back of the previous kernel's dirty lines, as in a training
 loop); `--flush-l2` instead evicts L2 between steps outside the events; barrier and
@@ -316,11 +318,38 @@ class L2Flush:
         torch.sum(self.r, dim=0, out=self.sink)
 
 
-def run_timed(wl, steps, warmup, dev, dist_on, flush_l2=False):
+def capture_graphs(fns, warmup):
+    """Each callable captured into its own CUDA graph (one memory pool), after
+    warm-up on the capture stream; returns the replay callables and the graphs."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    graphs = []
+    with torch.cuda.stream(s):
+        for _ in range(warmup):
+            for fn in fns:
+                fn()
+        pool = None
+        for fn in fns:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s, pool=pool):
+                fn()
+            pool = g.pool()
+            graphs.append(g)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    return [g.replay for g in graphs], graphs
+
+
+def run_timed(wl, steps, warmup, dev, dist_on, flush_l2=False, graphs=True):
     """Steps back to back (inputs larger than L2), or with an untimed L2Flush
-    between steps; CUDA events around every kernel."""
+    between steps; every kernel launched from its own CUDA graph (host
+    overhead off the device timeline) with CUDA events between them."""
     flush = L2Flush(dev) if flush_l2 else (lambda: None)
     ks = wl.kernels()
+    held = []
+    if graphs:
+        fns, held = capture_graphs([fn for _, fn, _ in ks], warmup)
+        ks = [(lab, f, b) for (lab, _, b), f in zip(ks, fns)]
     for _ in range(warmup):
         for _, fn, _ in ks:
             fn()
@@ -341,6 +370,7 @@ def run_timed(wl, steps, warmup, dev, dist_on, flush_l2=False):
     per_kernel = [sum(evs[k][i].elapsed_time(evs[k][i + 1]) for k in range(steps)) / steps
                   for i in range(len(ks))]
     step_ms = sum(per_kernel)
+    held.clear()  # graphs holding NCCL calls must go before the process group does
     return step_ms, per_kernel
 
 
@@ -464,6 +494,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--flush-l2", action="store_true", help="evict L2 between timed steps")
+    ap.add_argument("--eager", action="store_true",
+                    help="launch the timed kernels eagerly instead of from CUDA graphs")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -483,7 +515,8 @@ def main():
 
     wl = make_workload(args.workload, dev, seed=rank, world=world, rank=rank)
     with ClockSampler(local) as clk:
-        step_ms, per_kernel = run_timed(wl, args.steps, args.warmup, dev, dist_on, args.flush_l2)
+        step_ms, per_kernel = run_timed(wl, args.steps, args.warmup, dev, dist_on, args.flush_l2,
+                                        graphs=not args.eager)
     clocks = clk.summary()
     step_ms = max_over_ranks(step_ms, dist_on, dev)
     per_kernel = [max_over_ranks(v, dist_on, dev) for v in per_kernel]
@@ -521,7 +554,9 @@ def main():
                 "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
-                "config": dict(wl.config, parallelism=f"rows x{world}" if world > 1 else "1 GPU"),
+                "config": dict(wl.config, parallelism=f"rows x{world}" if world > 1 else "1 GPU",
+                               launch="eager" if args.eager else "CUDA graph per kernel",
+                               l2_flush=bool(args.flush_l2)),
                 "rows_per_s": world * wl.rows() / (step_ms * 1e-3),
                 "pct_of_peak": 100.0 * value / (world * peaks["hbm_gbs"]),
                 "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu, "e2e": e2e,

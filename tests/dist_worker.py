@@ -1,0 +1,61 @@
+"""Per-rank body of tests/test_gpu_dist.py (run under torchrun, one process per GPU).
+
+Each rank builds the same seeded inputs, takes its shard and checks the
+distributed result against the single-GPU kernels on the full input:
+  * vocab shards: ext.lse_partial on the local columns + NCCL all-gather of the
+    (max, sumexp) pairs + ext.lse_combine, fp16 logits of the LLM config shape
+    (rows scaled down);
+  * batch rows: robust fp32 forward on the local rows, gathered.
+Exits non-zero on any mismatch.
+"""
+import os
+import sys
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+
+
+def main():
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=60))
+    from fuselse_b200 import distributed as D, ext, workloads as W
+
+    G = dist.get_world_size()
+    # vocab shards of fp16 logits (B, 128256)
+    B, V = 256, 128256
+    logits = W.fp16_logits(B, V, seed=3, device=dev)
+    lo, hi = D.local_columns(V)
+    got = D.vocab_sharded_logsumexp(logits[:, lo:hi].contiguous())
+    want = ext.batched_logsumexp_fp16(logits)
+    err = ((got - want).abs() / want.abs().clamp_min(1.0)).max().item()
+    assert err <= 1e-5, f"vocab-shard combine err {err}"
+    # fp32 shards, robust rules across shards (-inf row, +inf in one shard)
+    x = W.fp32_rows(64, 40000, seed=4, device=dev)
+    x[3] = float("-inf")
+    x[5, 39999] = float("inf")
+    lo, hi = D.local_columns(x.size(1))
+    got = D.vocab_sharded_logsumexp(x[:, lo:hi].contiguous())
+    want = ext.onepass_lse_float_robust(x)
+    assert got[3] == float("-inf") and got[5] == float("inf")
+    fin = torch.isfinite(want)
+    err = ((got[fin] - want[fin]).abs() / want[fin].abs().clamp_min(1.0)).max().item()
+    assert err <= 1e-5, f"fp32 vocab-shard err {err}"
+    # batch rows
+    xb = W.fp32_rows(1000, 20000, seed=5, device=dev)
+    r0, r1 = D.local_rows(xb.size(0))
+    gathered = D.batch_sharded_logsumexp(xb[r0:r1], gather=True)
+    assert torch.equal(gathered, ext.onepass_lse_float_robust(xb)), "batch-shard gather differs"
+    dist.barrier()
+    if dist.get_rank() == 0:
+        print(f"dist ok: world {G}", flush=True)
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
