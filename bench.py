@@ -194,23 +194,30 @@ class F16Vocab(Workload):
     name = "f16_vocab"
     dtype = "f16"
 
-    def __init__(self, dev, seed, world=1, rank=0):
-        from fuselse_b200 import ext, workloads as W
+    def __init__(self, dev, seed, world=1, rank=0, nccl=False):
+        from fuselse_b200 import distributed as D, ext, workloads as W
         self.ext = ext
-        B, N, shards = 8192, 128256, 8
-        # this GPU's vocab shard of the (8192, 128256) logits; with fewer than 8
-        # GPUs every rank still processes one 16032-column shard per step
-        full = None
+        B = 8192
+        # this GPU's vocab shard of the (8192, 128256) logits (8 shards of 16032
+        # columns); with fewer than 8 GPUs every rank still holds one shard
         self.xs = W.fp16_logits(B, 16032, seed, dev)
         self.B, self.Ns = B, self.xs.size(1)
-        self.world = world
-        self.config = {"workload": "FuseLSE16 vocab shard (8192,16032) fp16 of (8192,128256); "
-                                   "partial (max,sumexp) + NCCL all-gather + combine",
+        self.world, self.nccl = world, nccl
+        if not nccl:
+            self.ex = (D.VocabShardExchange(B, device=dev) if world > 1
+                       else D.VocabShardExchange.single_rank(B, dev))
+        how = ("partial + NCCL all-gather + combine" if nccl else
+               "partial kernel storing (max,sumexp) into every rank's buffer over NVLink "
+               "+ flag-wait combine kernel")
+        self.config = {"workload": f"FuseLSE16 vocab shard (8192,16032) fp16 of (8192,128256); {how}",
                        "l2": "inputs larger than L2, steps back to back"}
         self.launches_per_step = 2
 
     def _step(self):
         from fuselse_b200 import distributed as D
+        if not self.nccl:
+            self.out = self.ex(self.xs)
+            return
         ms = self.ext.lse_partial(self.xs)
         if self.world > 1:
             self.out = self.ext.lse_combine(D.gather_partials(ms))
@@ -286,6 +293,8 @@ def make_workload(name, dev, seed, world, rank):
         return FwdBwdF32(dev, seed, do_bwd=False)
     if name == "f16_vocab":
         return F16Vocab(dev, seed, world, rank)
+    if name == "f16_vocab_nccl":
+        return F16Vocab(dev, seed, world, rank, nccl=True)
     if name == "intlse_q16":
         return IntLSE(dev, seed, "q16")
     if name == "intlse_q10_6":

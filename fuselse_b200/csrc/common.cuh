@@ -85,6 +85,29 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// 2^t on the FMA pipe, for t <= ~0 (used to offload part of the SFU work).
+// Range reduction: j = t + 1.5*2^23 rounds t to the nearest integer n, held in
+// j's low mantissa bits; f = t - n lies in [-1/2, 1/2].  2^f is a degree-5
+// polynomial whose coefficients were fitted here by the Remez exchange
+// algorithm on relative error (max 7.5e-8; 2.4e-7 with fp32 Horner rounding,
+// comparable to ex2.approx).  2^n is applied by adding n to the exponent field:
+// (bits(j) << 23) == n << 23 modulo 2^32.  t is clamped at -125 so the result
+// stays normal; inputs below contribute < 2^-125 of the largest term, and NaN
+// inputs are caught by the NaN-propagating running max, never by this value.
+__device__ __forceinline__ float ex2_poly(float t) {
+    t = fmaxf(t, -125.0f);
+    const float j = __fadd_rn(t, 12582912.0f);
+    const float n = __fsub_rn(j, 12582912.0f);
+    const float f = __fsub_rn(t, n);
+    float p = 0.0013276472454890609f;
+    p = fmaf(p, f, 0.009675540961325169f);
+    p = fmaf(p, f, 0.05550713092088699f);
+    p = fmaf(p, f, 0.24022120237350464f);
+    p = fmaf(p, f, 0.6931469440460205f);
+    p = fmaf(p, f, 1.0000001192092896f);
+    return __int_as_float(__float_as_int(p) + (__float_as_int(j) << 23));
+}
+
 // max that propagates NaN (PTX max.NaN.f32, sm_80+).
 __device__ __forceinline__ float max_nan(float a, float b) {
     float r;

@@ -16,6 +16,7 @@
 //   row-chunked grid (no per-element division), 16-byte load + 16-byte
 //   evict-first store per 4 elements, exp as FFMA + EX2.
 #include "common.cuh"
+#include "rows.cuh"
 
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
@@ -26,185 +27,6 @@ namespace cg = cooperative_groups;
 
 namespace fl {
 namespace {
-
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
-
-constexpr int kMaxSeg = 8;  // portable cluster size
-
-// Forward segment-kernel shape per element type (measured on B200): threads per
-// CTA, 16-byte vectors per thread per group, and whether the next group's
-// loads are issued before the current group is folded.  fp16 carries twice
-// the elements per byte, so it keeps more bytes in flight per thread.
-// Rows of at most kWarpRowBytes go one warp per row (no block barrier; kWarpU
-// vectors per lane per group, kWarpPipe as kPipe).
-// (fp16 defaults measured on B200 for (8192, 16032) vocab shards: warp per row,
-// 4 pipelined vectors per lane: 5.47 TB/s vs 4.26 TB/s for one 128-thread CTA
-// per row, whose end-of-row block barrier dominated.)
-#ifndef FL_F16_WARP_ROW_BYTES
-#define FL_F16_WARP_ROW_BYTES 65536
-#endif
-#ifndef FL_F16_WARP_U
-#define FL_F16_WARP_U 4
-#endif
-#ifndef FL_F16_WARP_PIPE
-#define FL_F16_WARP_PIPE 1
-#endif
-template <typename T>
-struct FwdShape;
-template <>
-struct FwdShape<float> {
-    static constexpr int kThreads = 256, kU = 4;
-    static constexpr bool kPipe = false;
-    static constexpr int64_t kWarpRowBytes = 16 * 1024;
-    static constexpr int kWarpU = 4;
-    static constexpr bool kWarpPipe = false;
-};
-template <>
-struct FwdShape<__half> {
-    static constexpr int kThreads = 128, kU = 8;
-    static constexpr bool kPipe = true;
-    static constexpr int64_t kWarpRowBytes = FL_F16_WARP_ROW_BYTES;
-    static constexpr int kWarpU = FL_F16_WARP_U;
-    static constexpr bool kWarpPipe = FL_F16_WARP_PIPE;
-};
-
-// Element traits: how many elements one 16-byte vector carries and how to
-// widen them to fp32.
-template <typename T>
-struct Elem;
-
-template <>
-struct Elem<float> {
-    static constexpr int kPerVec = 4;
-    __device__ __forceinline__ static float load1(const float* p) { return __ldg(p); }
-    __device__ __forceinline__ static void unpack(uint4 r, float* v) {
-        v[0] = __uint_as_float(r.x);
-        v[1] = __uint_as_float(r.y);
-        v[2] = __uint_as_float(r.z);
-        v[3] = __uint_as_float(r.w);
-    }
-};
-
-template <>
-struct Elem<__half> {
-    static constexpr int kPerVec = 8;
-    __device__ __forceinline__ static float load1(const __half* p) { return __half2float(__ldg(p)); }
-    __device__ __forceinline__ static void unpack(uint4 r, float* v) {
-        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
-            float2 f = __half22float2(h);
-            v[2 * i] = f.x;
-            v[2 * i + 1] = f.y;
-        }
-    }
-};
-
-// Fold K values into the thread state (m, s): one max tree, one rescale,
-// K EX2s summed into two partial accumulators.
-template <int K>
-__device__ __forceinline__ void ms_fold(float& m, float& s, const float* v) {
-    float t[K];
-#pragma unroll
-    for (int i = 0; i < K; ++i) t[i] = v[i];
-#pragma unroll
-    for (int w = 1; w < K; w *= 2)
-#pragma unroll
-        for (int i = 0; i + w < K; i += 2 * w) t[i] = max_nan(t[i], t[i + w]);
-    const float M = max_nan(m, t[0]);
-    const float Ml = safe_max(M) * kLog2e;
-    float a0 = s * ex2(fmaf(m, kLog2e, -Ml));
-    float a1 = 0.0f;
-#pragma unroll
-    for (int i = 0; i < K; i += 2) {
-        a0 += ex2(fmaf(v[i], kLog2e, -Ml));
-        if (i + 1 < K) a1 += ex2(fmaf(v[i + 1], kLog2e, -Ml));
-    }
-    s = a0 + a1;
-    m = M;
-}
-
-__device__ __forceinline__ void ms_fold1(float& m, float& s, float v) {
-    ms_merge(m, s, v, v == -INFINITY ? 0.0f : 1.0f);
-}
-
-// Misalignment prefix: elements before the first 16-byte boundary of a row.
-template <typename T>
-__device__ __forceinline__ int64_t head_elems(const T* rowp, int64_t N) {
-    const uint32_t mis = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(rowp) & 15u);
-    int64_t p = mis ? static_cast<int64_t>((16u - mis) / sizeof(T)) : 0;
-    return p < N ? p : N;
-}
-
-// Accumulate vectors [v0, v1) of a row (vector i starts at element head + i*E)
-// with `stride` threads, this thread starting at `first`.
-template <typename T, int U, bool PIPE>
-__device__ __forceinline__ void fold_vectors(const T* vbase, int64_t v0, int64_t v1,
-                                             int first, int stride, float& m, float& s) {
-    constexpr int E = Elem<T>::kPerVec;
-    const uint4* vp = reinterpret_cast<const uint4*>(vbase);
-    int64_t i = v0 + first;
-    // software pipeline: the next U vectors are in flight while this group folds
-    const int64_t step = (int64_t)U * stride;
-    if (PIPE && i + (int64_t)(U - 1) * stride < v1) {
-        uint4 cur[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) cur[u] = ld_stream_u4(vp + i + (int64_t)u * stride);
-        for (i += step; i + (int64_t)(U - 1) * stride < v1; i += step) {
-            uint4 nxt[U];
-#pragma unroll
-            for (int u = 0; u < U; ++u) nxt[u] = ld_stream_u4(vp + i + (int64_t)u * stride);
-            float v[U * E];
-#pragma unroll
-            for (int u = 0; u < U; ++u) Elem<T>::unpack(cur[u], v + u * E);
-            ms_fold<U * E>(m, s, v);
-#pragma unroll
-            for (int u = 0; u < U; ++u) cur[u] = nxt[u];
-        }
-        float v[U * E];
-#pragma unroll
-        for (int u = 0; u < U; ++u) Elem<T>::unpack(cur[u], v + u * E);
-        ms_fold<U * E>(m, s, v);
-    }
-    for (; i + (int64_t)(U - 1) * stride < v1; i += step) {
-        uint4 r[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) r[u] = ld_stream_u4(vp + i + (int64_t)u * stride);
-        float v[U * E];
-#pragma unroll
-        for (int u = 0; u < U; ++u) Elem<T>::unpack(r[u], v + u * E);
-        ms_fold<U * E>(m, s, v);
-    }
-    for (; i < v1; i += stride) {
-        float v[E];
-        Elem<T>::unpack(ld_stream_u4(vp + i), v);
-        ms_fold<E>(m, s, v);
-    }
-}
-
-// Block-wide merge; the result is valid in thread 0.
-template <int THREADS>
-__device__ __forceinline__ void ms_block_reduce(float& m, float& s) {
-    constexpr int kWarps = THREADS / 32;
-    __shared__ float2 part[kWarps];
-    ms_warp_allreduce(m, s);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0) part[warp] = make_float2(m, s);
-    __syncthreads();
-    if (warp == 0) {
-        float2 p = lane < kWarps ? part[lane] : make_float2(-INFINITY, 0.0f);
-        m = p.x;
-        s = p.y;
-#pragma unroll
-        for (int off = kWarps / 2; off > 0; off >>= 1) {
-            const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
-            const float s2 = __shfl_xor_sync(0xffffffffu, s, off);
-            ms_merge(m, s, m2, s2);
-        }
-    }
-}
 
 // One CTA per row segment; the nseg CTAs of a row form one cluster.
 // PARTIAL: write (m, s) pairs instead of the finished value.
@@ -262,19 +84,11 @@ template <typename T, bool PARTIAL>
 __global__ void __launch_bounds__(kThreads) lse_warp_kernel(
     const T* __restrict__ x, float* __restrict__ out, int64_t B, int64_t N,
     float empty_value) {
-    constexpr int E = Elem<T>::kPerVec;
     const int lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
     if (row >= B) return;
-    const T* rowp = x + row * N;
-    const int64_t head = head_elems(rowp, N);
-    const int64_t nv = (N - head) / E;
-    const int64_t tail0 = head + nv * E;
-    float m = -INFINITY, s = 0.0f;
-    fold_vectors<T, FwdShape<T>::kWarpU, FwdShape<T>::kWarpPipe>(rowp + head, 0, nv, lane, 32, m, s);
-    if (lane < head) ms_fold1(m, s, Elem<T>::load1(rowp + lane));
-    if (tail0 + lane < N) ms_fold1(m, s, Elem<T>::load1(rowp + tail0 + lane));
-    ms_warp_allreduce(m, s);
+    float m, s;
+    fold_row_warp(x + row * N, N, lane, m, s);
     if (lane == 0) {
         if (PARTIAL) {
             reinterpret_cast<float2*>(out)[row] = make_float2(m, s);

@@ -1,0 +1,200 @@
+// Vocab-sharded log-sum-exp with the exchange done by the kernels themselves
+// over NVLink peer memory (no NCCL on the data path).
+//
+// Each of G ranks holds the same B rows restricted to its own columns.
+//   kernel 1 (vocab_scatter_kernel): one warp per row folds the local columns
+//     into (m, s) = (max, sum exp(x - m)) and stores the pair straight into
+//     every rank's exchange buffer (P2P stores through the peer mappings of a
+//     symmetric allocation); the last of its CTAs fences at system scope and
+//     adds 1 to this rank's counter in every rank's flag array (release,
+//     system scope), so a counter equals the number of calls delivered;
+//   kernel 2 (vocab_combine_kernel, one thread per row): every CTA waits until
+//     every rank's counter shows this call's contributions (acquire, system
+//     scope; bounded by an iteration cap and a 2 s clock limit, after which it
+//     writes NaN rows and sets a sticky error word), merges the G pairs of each
+//     row and finishes lse = M + log(sum_g s_g exp(m_g - M)); the last CTA to
+//     finish advances the call epoch.
+// The epoch lives in the buffer, so captured CUDA graphs replay correctly;
+// pairs alternate between two slots by epoch parity, so a rank that starts the
+// next call cannot overwrite pairs another rank is still reading (it can only
+// get one call ahead).  Every rank must make the same sequence of calls with
+// the same B.
+//
+// Exchange buffer layout (identical on all ranks, 256-byte aligned):
+//   [0, 256)                 header: finished epoch, sticky error, epoch in
+//                            flight, combine CTAs done (u32 each)
+//   [256, 256 + F)           flags: G x u32, F = G*4 rounded up to 256
+//   [256 + F, ...)           pairs: [2 slots][G ranks][B rows] float2
+#include "common.cuh"
+#include "rows.cuh"
+
+#include <cuda_fp16.h>
+
+namespace fl {
+namespace {
+
+constexpr int kRowsPerCta = 8;  // one warp per row
+constexpr int64_t kHeaderBytes = 256;
+
+__host__ __device__ inline int64_t flags_bytes(int64_t G) { return (G * 4 + 255) / 256 * 256; }
+__host__ __device__ inline int64_t pairs_offset(int64_t G) { return kHeaderBytes + flags_bytes(G); }
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void red_release_sys_add(uint32_t* p, uint32_t v) {
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Header words (local use): [0] epoch of the last finished call, [1] sticky
+// error, [2] epoch of the call in flight (written by the scatter kernel, read
+// by every combine CTA), [3] combine CTAs finished and [4] scatter CTAs
+// finished in the call in flight (both reset by the last CTA).
+template <typename T>
+__global__ void __launch_bounds__(kRowsPerCta * 32) vocab_scatter_kernel(
+    const T* __restrict__ x, int64_t B, int64_t N, unsigned char* const* __restrict__ peers,
+    unsigned char* __restrict__ local, int rank, int G) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (int64_t)blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
+    uint32_t* header = reinterpret_cast<uint32_t*>(local);
+    const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(header) + 1;
+    const int64_t slot = epoch & 1u;
+    if (blockIdx.x == 0 && threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(header + 2) = epoch;
+    if (row < B) {
+        float m, s;
+        fold_row_warp(x + row * N, N, lane, m, s);
+        // lanes 0..G-1 each deliver the pair to one rank
+        for (int p = lane; p < G; p += 32) {
+            float2* dst = reinterpret_cast<float2*>(peers[p] + pairs_offset(G)) +
+                          ((slot * G + rank) * B + row);
+            *dst = make_float2(m, s);
+        }
+    }
+    // Publication, one system-scope fence per call: the barrier orders this
+    // CTA's stores before thread 0's GPU-scope release (fence + count); the
+    // last CTA to count has observed every CTA's release, so its system-scope
+    // fence — cumulative — orders all of the call's stores before the
+    // release adds that tell the peers this rank's pairs are in place.
+    __shared__ int last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        last = atomicAdd(header + 4, 1u) == gridDim.x - 1;
+        if (last) {
+            header[4] = 0;
+            __threadfence_system();
+        }
+    }
+    __syncthreads();
+    if (last && threadIdx.x < G) {
+        uint32_t* flags = reinterpret_cast<uint32_t*>(peers[threadIdx.x] + kHeaderBytes);
+        red_release_sys_add(flags + rank, 1u);
+    }
+}
+
+constexpr int kCombineThreads = 256;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr uint32_t kWaitLimitIters = 1u << 26;
+
+// One thread per row; every CTA waits for the flags itself.  The last CTA to
+// finish advances the finished-call epoch.
+__global__ void __launch_bounds__(kCombineThreads) vocab_combine_kernel(
+    unsigned char* __restrict__ local, float* __restrict__ out, int64_t B, int G, uint32_t ngroups) {
+    __shared__ int timed_out;
+    uint32_t* header = reinterpret_cast<uint32_t*>(local);
+    const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(header + 2);
+    const uint32_t expected = epoch;  // every rank adds 1 per call
+    if (threadIdx.x == 0) timed_out = 0;
+    __syncthreads();
+    if (threadIdx.x < G) {
+        const uint32_t* flag = reinterpret_cast<const uint32_t*>(local + kHeaderBytes) + threadIdx.x;
+        const uint64_t t0 = global_ns();
+        for (uint32_t it = 0;; ++it) {
+            if ((int32_t)(ld_acquire_sys(flag) - expected) >= 0) break;
+            if (it >= kWaitLimitIters || global_ns() - t0 > kWaitLimitNs) {
+                atomicExch(&timed_out, 1);
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    __syncthreads();
+    const int bad = timed_out;
+    const int64_t slot = epoch & 1u;
+    const float2* pairs = reinterpret_cast<const float2*>(local + pairs_offset(G)) + slot * G * B;
+    const int64_t r = (int64_t)blockIdx.x * kCombineThreads + threadIdx.x;
+    if (r < B) {
+        if (bad) {
+            out[r] = __int_as_float(0x7fc00000);
+        } else {
+            float m = -INFINITY, s = 0.0f;
+            for (int q = 0; q < G; ++q) {
+                const float2 p = __ldcv(pairs + (int64_t)q * B + r);  // written by peers
+                ms_merge(m, s, p.x, p.y);
+            }
+            out[r] = ms_finalize(m, s, -INFINITY);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (bad) atomicExch(header + 1, 1u);
+        __threadfence();
+        if (atomicAdd(header + 3, 1u) == gridDim.x - 1) {  // last CTA of this call
+            header[3] = 0;
+            *reinterpret_cast<volatile uint32_t*>(header) = epoch;
+        }
+    }
+}
+
+}  // namespace
+}  // namespace fl
+
+using namespace fl;
+
+extern "C" int fl_vocab_exchange_bytes(int64_t G, int64_t B, int64_t* bytes) {
+    clear_error();
+    FL_REQUIRE(G >= 1 && G <= 1024 && B >= 0 && bytes, "fl_vocab_exchange_bytes: bad arguments");
+    *bytes = pairs_offset(G) + 2 * G * B * (int64_t)sizeof(float2);
+    return FL_OK;
+}
+
+extern "C" int fl_lse_vocab_exchange(const void* x, int dtype, int64_t B, int64_t N,
+                                     void* const* peer_bufs, void* local_buf, int rank, int G,
+                                     float* out, fl_stream_t stream) {
+    clear_error();
+    const char* what = "fl_lse_vocab_exchange";
+    FL_REQUIRE(dtype == 0 || dtype == 1, "%s: dtype must be 0 (fp32) or 1 (fp16)", what);
+    FL_REQUIRE(B >= 0 && N >= 0, "%s: negative shape", what);
+    FL_REQUIRE(G >= 1 && G <= 1024 && rank >= 0 && rank < G, "%s: rank %d of %d invalid", what, rank, G);
+    FL_REQUIRE(peer_bufs && local_buf && (B == 0 || out), "%s: NULL buffer", what);
+    FL_REQUIRE(B == 0 || N == 0 || x, "%s: x is NULL", what);
+    FL_REQUIRE(aligned_to(local_buf, 256), "%s: exchange buffer must be 256-byte aligned", what);
+    FL_REQUIRE(aligned_to(x, dtype == 0 ? 4 : 2) && aligned_to(out, 4), "%s: misaligned buffer", what);
+    const int64_t ngroups = (B + kRowsPerCta - 1) / kRowsPerCta;
+    FL_REQUIRE(ngroups <= INT32_MAX, "%s: B too large", what);
+    if (B == 0) return FL_OK;  // every rank has B == 0: no call, no epoch
+    if (int st = bind_device(stream, local_buf)) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    auto peers = reinterpret_cast<unsigned char* const*>(peer_bufs);
+    auto local = reinterpret_cast<unsigned char*>(local_buf);
+    if (dtype == 0)
+        vocab_scatter_kernel<float><<<(unsigned)ngroups, kRowsPerCta * 32, 0, s>>>(
+            reinterpret_cast<const float*>(x), B, N, peers, local, rank, G);
+    else
+        vocab_scatter_kernel<__half><<<(unsigned)ngroups, kRowsPerCta * 32, 0, s>>>(
+            reinterpret_cast<const __half*>(x), B, N, peers, local, rank, G);
+    if (int st = check_launch(what)) return st;
+    const int64_t cgrid = (B + kCombineThreads - 1) / kCombineThreads;
+    vocab_combine_kernel<<<(unsigned)cgrid, kCombineThreads, 0, s>>>(local, out, B, G,
+                                                                     (uint32_t)ngroups);
+    return check_launch(what);
+}

@@ -8,10 +8,14 @@ Two layouts (the reference itself is single-GPU; both are additions):
   on their rank unless the caller gathers them.
 
 * Vocab shards (LLM logits split along N across ranks): each rank reduces its
-  columns to per-row partial states (m, s) = (max, sum exp(x - m)) with
-  ext.lse_partial, the ranks exchange the 8-byte states of every row with one
-  all-gather (NCCL over NVLink), and each rank combines the G states of a row
-  locally (ext.lse_combine):  lse = M + log(sum_g s_g exp(m_g - M)).
+  columns to per-row partial states (m, s) = (max, sum exp(x - m)), the ranks
+  exchange the 8-byte states of every row, and each rank combines the G states
+  of a row locally:  lse = M + log(sum_g s_g exp(m_g - M)).  Two exchanges:
+  VocabShardExchange (the product path) has the partial kernel store the pairs
+  straight into every rank's buffer over NVLink and signal with system-scope
+  atomics, then a combine kernel waits for all ranks; vocab_sharded_logsumexp
+  does the same with ext.lse_partial, an NCCL all-gather and ext.lse_combine
+  (the baseline, and the path for groups without peer memory).
   Every rank ends with the full (B,) result.  The association differs from a
   single-GPU pass, so results agree to rounding, not bit for bit.
 
@@ -73,6 +77,84 @@ def vocab_sharded_logsumexp(x_shard: torch.Tensor, group=None,
     if ms.dim() != 2 or ms.size(1) != 2:
         raise RuntimeError("partial state must be (B, 2)")
     return combine_fn(gather_partials(ms, group))
+
+
+class VocabShardExchange:
+    """Vocab-sharded log-sum-exp with the (max, sumexp) exchange done by this
+    library's own kernels over NVLink peer memory (fl_lse_vocab_exchange): the
+    partial kernel stores each row's pair into every rank's exchange buffer
+    and signals with system-scope atomics; a combine kernel waits (bounded)
+    for all ranks and finishes the rows.  No NCCL call on the data path.
+
+    The exchange buffer is a torch symmetric-memory allocation (peer mappings
+    of every rank's buffer on every device), made once per (group, rows).
+    Every rank must call with the same B, in the same sequence.
+    """
+
+    def __init__(self, rows: int, group=None, device=None):
+        import ctypes
+
+        import torch.distributed._symmetric_memory as symm
+
+        from . import _lib
+        self.group = group if group is not None else dist.group.WORLD
+        self.G = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        self.rows = rows
+        self.device = torch.device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device())
+        nbytes = ctypes.c_int64()
+        _lib.call("fl_vocab_exchange_bytes", self.G, rows, ctypes.byref(nbytes))
+        self.buf = symm.empty(nbytes.value, dtype=torch.uint8, device=self.device)
+        self.buf.zero_()
+        torch.cuda.synchronize(self.device)
+        try:
+            self.handle = symm.rendezvous(self.buf, self.group)
+        except RuntimeError:
+            symm.enable_symm_mem_for_group(self.group.group_name)
+            self.handle = symm.rendezvous(self.buf, self.group)
+        self.peer_array = self.handle.buffer_ptrs_dev
+        dist.barrier(self.group)  # every rank's buffer is zeroed before anyone writes
+
+    @classmethod
+    def single_rank(cls, rows: int, device="cuda"):
+        """G = 1 exchange on one GPU, without a process group (tests, 1-GPU runs)."""
+        import ctypes
+
+        from . import _lib
+        self = cls.__new__(cls)
+        self.group, self.G, self.rank, self.rows = None, 1, 0, rows
+        self.device = torch.device(device)
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        nbytes = ctypes.c_int64()
+        _lib.call("fl_vocab_exchange_bytes", 1, rows, ctypes.byref(nbytes))
+        self.buf = torch.zeros(nbytes.value, dtype=torch.uint8, device=self.device)
+        self._ptrs = torch.tensor([self.buf.data_ptr()], dtype=torch.int64, device=self.device)
+        self.peer_array = self._ptrs.data_ptr()
+        return self
+
+    def __call__(self, x_shard: torch.Tensor) -> torch.Tensor:
+        import ctypes
+
+        from . import _lib
+        if x_shard.dim() != 2 or x_shard.size(0) != self.rows:
+            raise RuntimeError(f"expected a ({self.rows}, N) shard, got {tuple(x_shard.shape)}")
+        if not (x_shard.is_cuda and x_shard.device == self.device and x_shard.is_contiguous()):
+            raise RuntimeError(f"shard must be contiguous on {self.device}")
+        if x_shard.dtype not in (torch.float32, torch.float16):
+            raise RuntimeError("shard must be fp32 or fp16")
+        out = torch.empty(self.rows, dtype=torch.float32, device=self.device)
+        stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        _lib.call("fl_lse_vocab_exchange", ctypes.c_void_p(x_shard.data_ptr()),
+                  0 if x_shard.dtype == torch.float32 else 1, self.rows, x_shard.size(1),
+                  ctypes.c_void_p(self.peer_array), ctypes.c_void_p(self.buf.data_ptr()),
+                  self.rank, self.G, _lib.ptr(out), stream)
+        return out
+
+    def error(self) -> bool:
+        """True once a combine gave up waiting for a peer (sticky)."""
+        return bool(self.buf[4:8].view(torch.int32).item())
 
 
 def batch_sharded_logsumexp(x_local: torch.Tensor, robust: bool = True,

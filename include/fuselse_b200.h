@@ -90,6 +90,25 @@ int fl_lse_combine(const float* ms, float* out, int64_t G, int64_t B,
                    fl_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Vocab-sharded log-sum-exp with the exchange done over NVLink peer memory
+ * (no reference counterpart; the reference is single-GPU).  G ranks hold
+ * the same B rows split by columns; rank `rank` passes its (B, N) shard x
+ * (dtype 0: fp32, 1: fp16).  `local_buf` is this rank's exchange buffer of
+ * fl_vocab_exchange_bytes(G, B) bytes (256-byte aligned, zero-filled once
+ * before first use on every rank, then left to the library), and
+ * `peer_bufs` a DEVICE array of the G ranks' buffer addresses as mapped on
+ * this device (a symmetric allocation; peer_bufs[rank] == local_buf).
+ * Writes out (B,) fp32 on every rank.  Every rank must make the same
+ * sequence of calls with the same B.  If a peer's contribution does not
+ * arrive within 2 s the rows are NaN and the 32-bit word at byte offset 4
+ * of local_buf becomes non-zero (sticky).
+ * ---------------------------------------------------------------------- */
+int fl_vocab_exchange_bytes(int64_t G, int64_t B, int64_t* bytes);
+int fl_lse_vocab_exchange(const void* x, int dtype, int64_t B, int64_t N,
+                          void* const* peer_bufs, void* local_buf, int rank, int G,
+                          float* out, fl_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * IntLSE Q16.16 with fp32 base-e input: q = rint_sat(x * log2(e) * 2^16),
  * pairwise base-2 Mitchell reduction with the 64-entry correction table
  * (use_lut != 0) or without it (use_lut == 0), out = acc * ln2 / 2^16.

@@ -46,6 +46,38 @@ def main():
     fin = torch.isfinite(want)
     err = ((got[fin] - want[fin]).abs() / want[fin].abs().clamp_min(1.0)).max().item()
     assert err <= 1e-5, f"fp32 vocab-shard err {err}"
+    # the same through the library's own NVLink exchange (peer stores + flags),
+    # several calls in a row (epochs, slot alternation) and from a CUDA graph
+    ex = D.VocabShardExchange(B, device=dev)
+    lo, hi = D.local_columns(V)
+    shard = logits[:, lo:hi].contiguous()
+    want16 = ext.batched_logsumexp_fp16(logits)
+    for _ in range(3):
+        got = ex(shard)
+        err = ((got - want16).abs() / want16.abs().clamp_min(1.0)).max().item()
+        assert err <= 1e-5, f"peer exchange err {err}"
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        ex(shard)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            g_out = ex(shard)
+    torch.cuda.current_stream().wait_stream(s)
+    for _ in range(3):
+        g_out.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        err = ((g_out - want16).abs() / want16.abs().clamp_min(1.0)).max().item()
+        assert err <= 1e-5, f"peer exchange (graph replay) err {err}"
+    del graph
+    ex32 = D.VocabShardExchange(x.size(0), device=dev)
+    lo, hi = D.local_columns(x.size(1))
+    got = ex32(x[:, lo:hi].contiguous())
+    assert got[3] == float("-inf") and got[5] == float("inf")
+    err = ((got[fin] - want[fin]).abs() / want[fin].abs().clamp_min(1.0)).max().item()
+    assert err <= 1e-5, f"fp32 peer exchange err {err}"
+    assert not ex.error() and not ex32.error()
     # batch rows
     xb = W.fp32_rows(1000, 20000, seed=5, device=dev)
     r0, r1 = D.local_rows(xb.size(0))

@@ -190,3 +190,28 @@ def test_partial_combine_equals_full_row(ext, dtype, G):
     parts = [ext.lse_partial(x[:, a:b].contiguous()) for a, b in zip(cols, cols[1:])]
     got = ext.lse_combine(torch.stack(parts)).cpu().numpy()
     _close(got, O.lse_f64(x.float().cpu().numpy()), RTOL32, f"G={G}")
+
+
+# ------------------------------------------------ peer-memory exchange, G = 1
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+@pytest.mark.parametrize("B,N", [(1, 5), (7, 16032), (8192, 16032), (13, 100003)])
+def test_vocab_exchange_single_rank(ext, dtype, B, N):
+    from fuselse_b200.distributed import VocabShardExchange
+    ex = VocabShardExchange.single_rank(B)
+    x = _randn(B, N, seed=B + N, scale=3.0).to(dtype)
+    if B > 3:
+        x[2] = float("-inf")
+    want = O.lse_f64(x.float().cpu().numpy())
+    for _ in range(3):  # epochs advance, slots alternate
+        _close(ex(x).cpu().numpy(), want, RTOL32, f"exchange {B}x{N}")
+    assert not ex.error()
+    assert ex.buf[:4].view(torch.int32).item() == 3  # epoch counter
+
+
+def test_vocab_exchange_rejects_bad_shapes(ext):
+    from fuselse_b200.distributed import VocabShardExchange
+    ex = VocabShardExchange.single_rank(4)
+    with pytest.raises(RuntimeError):
+        ex(torch.zeros(5, 10, device="cuda"))
+    with pytest.raises(RuntimeError):
+        ex(torch.zeros(4, 10, device="cuda", dtype=torch.float64))
