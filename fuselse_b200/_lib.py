@@ -41,6 +41,7 @@ SIGNATURES = {
     "fl_vocab_exchange_bytes": [c_int64, c_int64, POINTER(c_int64)],
     "fl_lse_vocab_exchange": [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_int, c_int,
                               _fp, _stream],
+    "fl_lse_vocab_exchange_noalloc": [c_void_p, c_int, c_int64, c_int64, _fp, _stream],
 }
 
 

@@ -198,3 +198,87 @@ extern "C" int fl_lse_vocab_exchange(const void* x, int dtype, int64_t B, int64_
                                                                      (uint32_t)ngroups);
     return check_launch(what);
 }
+
+// ---------------------------------------------------------------------------
+// No-allocation variant (one device).  Some callers cannot allocate device
+// memory at all: a host whose GPU is driven through a plugin or embedded
+// runtime that owns every allocation, or code whose memory budget is fixed
+// before these calls.  For them the exchange buffer of the single-rank
+// (G = 1) exchange is a file-scope array: every device that loads this
+// library holds kNoAllocBytes of it until the process exits.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace fl {
+namespace {
+
+constexpr int64_t kNoAllocBytes = 4 << 20;  // per device
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_noalloc_exchange[kNoAllocBytes];
+static __device__ __align__(256) unsigned char* g_noalloc_peers[1];
+
+struct NoAllocDevice {
+    bool ready = false;
+    unsigned char* exchange = nullptr;  // device address of g_noalloc_exchange
+    unsigned char** peers = nullptr;    // device address of g_noalloc_peers
+};
+
+std::mutex g_noalloc_mu;
+NoAllocDevice g_noalloc[kNoAllocMaxDevices];
+
+// Once per device, with that device current.  In host code the arrays' names
+// are only stand-ins, so their device addresses come from
+// cudaGetSymbolAddress; the epochs and counters are cleared (the pairs need
+// not be) and the one-entry peer table points at this device's own array.
+int noalloc_setup(int dev) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    NoAllocDevice& d = g_noalloc[dev];
+    if (d.ready) return FL_OK;
+    FL_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&d.exchange), g_noalloc_exchange));
+    FL_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&d.peers), g_noalloc_peers));
+    FL_CUDA(cudaMemset(d.exchange, 0, kHeaderBytes + flags_bytes(1)));
+    FL_CUDA(cudaMemcpyToSymbol(g_noalloc_peers, &d.exchange, sizeof(unsigned char*)));
+    FL_CUDA(cudaDeviceSynchronize());
+    d.ready = true;
+    return FL_OK;
+}
+
+}  // namespace
+}  // namespace fl
+
+extern "C" int fl_lse_vocab_exchange_noalloc(const void* x, int dtype, int64_t B, int64_t N,
+                                             float* out, fl_stream_t stream) {
+    clear_error();
+    const char* what = "fl_lse_vocab_exchange_noalloc";
+    FL_REQUIRE(dtype == 0 || dtype == 1, "%s: dtype must be 0 (fp32) or 1 (fp16)", what);
+    FL_REQUIRE(B >= 0 && N >= 0, "%s: negative shape", what);
+    const int64_t need = pairs_offset(1) + 2 * B * (int64_t)sizeof(float2);
+    const int64_t max_rows = (kNoAllocBytes - pairs_offset(1)) / (2 * (int64_t)sizeof(float2));
+    FL_REQUIRE(need <= kNoAllocBytes,
+               "%s: B=%lld rows exceed the static exchange buffer (%lld bytes, at most %lld rows)",
+               what, (long long)B, (long long)kNoAllocBytes, (long long)max_rows);
+    FL_REQUIRE(B == 0 || out, "%s: out is NULL", what);
+    FL_REQUIRE(B == 0 || N == 0 || x, "%s: x is NULL", what);
+    FL_REQUIRE(aligned_to(x, dtype == 0 ? 4 : 2) && aligned_to(out, 4), "%s: misaligned buffer", what);
+    if (B == 0) return FL_OK;
+    if (int st = bind_device(stream, out)) return st;
+    int dev = -1;
+    FL_CUDA(cudaGetDevice(&dev));
+    FL_REQUIRE(dev >= 0 && dev < kNoAllocMaxDevices, "%s: device %d out of range", what, dev);
+    if (int st = noalloc_setup(dev)) return st;
+    const NoAllocDevice& d = g_noalloc[dev];
+    const int64_t ngroups = (B + kRowsPerCta - 1) / kRowsPerCta;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (dtype == 0)
+        vocab_scatter_kernel<float><<<(unsigned)ngroups, kRowsPerCta * 32, 0, s>>>(
+            reinterpret_cast<const float*>(x), B, N, d.peers, d.exchange, 0, 1);
+    else
+        vocab_scatter_kernel<__half><<<(unsigned)ngroups, kRowsPerCta * 32, 0, s>>>(
+            reinterpret_cast<const __half*>(x), B, N, d.peers, d.exchange, 0, 1);
+    if (int st = check_launch(what)) return st;
+    const int64_t cgrid = (B + kCombineThreads - 1) / kCombineThreads;
+    vocab_combine_kernel<<<(unsigned)cgrid, kCombineThreads, 0, s>>>(d.exchange, out, B, 1,
+                                                                     (uint32_t)ngroups);
+    return check_launch(what);
+}

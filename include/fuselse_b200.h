@@ -109,6 +109,26 @@ int fl_lse_vocab_exchange(const void* x, int dtype, int64_t B, int64_t N,
                           float* out, fl_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * The single-rank (G = 1) fl_lse_vocab_exchange without any device
+ * allocation (no counterpart in the reference).  For callers that cannot
+ * allocate device memory: a host whose GPU is driven through a plugin or
+ * embedded runtime that owns every allocation, or code whose memory budget
+ * is fixed before these calls.  Instead of a caller buffer, the exchange
+ * buffer is a file-scope array compiled into this library: 4 MiB per
+ * device, held by every GPU that loads the library until the process exits.
+ * Limit: B <= 262,112 rows (larger requests are rejected with
+ * FL_ERR_INVALID_ARGUMENT and a message giving the maximum).  x (B, N) of
+ * dtype 0 (fp32) or 1 (fp16), out (B,) fp32, on the device of `stream`.
+ * The first call on a device resolves the array's device address, clears
+ * its counters and synchronizes the device: make it before any stream
+ * capture.  All calls on a device share the array, which keeps the last
+ * call's contents: calls that overlap on a GPU (other streams, other
+ * threads) race and must not be issued.
+ * ---------------------------------------------------------------------- */
+int fl_lse_vocab_exchange_noalloc(const void* x, int dtype, int64_t B, int64_t N,
+                                  float* out, fl_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * IntLSE Q16.16 with fp32 base-e input: q = rint_sat(x * log2(e) * 2^16),
  * pairwise base-2 Mitchell reduction with the 64-entry correction table
  * (use_lut != 0) or without it (use_lut == 0), out = acc * ln2 / 2^16.
