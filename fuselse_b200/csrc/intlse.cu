@@ -16,9 +16,11 @@
 //     leader CTA's shared memory through DSMEM;
 //   * the correction table lives in shared memory replicated per lane
 //     (conflict-free) instead of __constant__ with divergent indices;
-//   * the pair step is the shorter-chain restatement of intlse.cuh, and the
-//     table read is skipped for a whole warp when no lane can need it;
-//   * each chain keeps D vectors of its row in flight in registers.
+//   * the pair step is the shorter-chain restatement of intlse.cuh;
+//   * each chain keeps D rounds of its row in flight in registers, and the
+//     full rounds run without per-step predicates (a warp vote that skipped
+//     the table read when no lane needed it was measured: its branch forced
+//     waits on the in-flight loads and made long rows 2.5x slower).
 #include "common.cuh"
 #include "intlse.cuh"
 
@@ -31,8 +33,10 @@ namespace {
 
 enum Kind { kQ16F32 = 0, kQ16I32 = 1, kQ106I16 = 2 };
 
+// Rounds in flight per chain for long rows (measured on B200 for (64, 1048576):
+// 8 -> 0.187 ms, 16 -> 0.171 ms, 24 -> 0.157 ms for Q16.16).
 #ifndef FL_INTLSE_DLONG
-#define FL_INTLSE_DLONG 32
+#define FL_INTLSE_DLONG 24
 #endif
 
 // Reference constants (lse_kernel.cu:23-27): CONV = LOG2_E * 2^16 and
@@ -79,19 +83,19 @@ struct Q4 {
 };
 
 template <int KIND>
-__device__ __forceinline__ Q4 load_vec(const typename IK<KIND>::In* base, int64_t i) {
+__device__ __forceinline__ Q4 load_vec_at(const typename IK<KIND>::In* v) {
     Q4 q;
     if constexpr (KIND == kQ106I16) {
         uint32_t a, b;
         asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
                      : "=r"(a), "=r"(b)
-                     : "l"(base + 4 * i));
+                     : "l"(v));
         q.v[0] = (int)(int16_t)(a & 0xffffu);
         q.v[1] = (int)a >> 16;
         q.v[2] = (int)(int16_t)(b & 0xffffu);
         q.v[3] = (int)b >> 16;
     } else {
-        const uint4 r = ld_stream_u4(base + 4 * i);
+        const uint4 r = ld_stream_u4(v);
         q.v[0] = IK<KIND>::conv(r.x);
         q.v[1] = IK<KIND>::conv(r.y);
         q.v[2] = IK<KIND>::conv(r.z);
@@ -121,9 +125,6 @@ __global__ void __launch_bounds__(CTA) intlse_rows_kernel(
     using In = typename IK<KIND>::In;
     constexpr int F = IK<KIND>::F;
     constexpr int C = 256 / CTA;
-    // long chains (D > 4) take the warp-uniform table skip; short ones need the
-    // table too often for the vote to pay
-    constexpr bool kSkip = D > 4;
     __shared__ __align__(16) int lut_s[64 * 32];
     __shared__ int warp_val[8];
 
@@ -142,7 +143,6 @@ __global__ void __launch_bounds__(CTA) intlse_rows_kernel(
     const int64_t head = head_count<KIND>(rowp, N);
     const int64_t nv = (N - head) / 4;
     const int64_t tail0 = head + nv * 4;
-    const int64_t K = (nv + 255) / 256;  // vector steps, uniform over the row
     const In* vbase = rowp + head;
 
     int acc = kQNegInf;
@@ -153,39 +153,50 @@ __global__ void __launch_bounds__(CTA) intlse_rows_kernel(
     }
     // vector step 0 carries the seed when there was no head element
     if (t < nv) {
-        const Q4 q = load_vec<KIND>(vbase, t);
+        const Q4 q = load_vec_at<KIND>(vbase + 4 * (int64_t)t);
         acc = has ? pair_exact<F, LUT>(acc, q.v[0], lut) : q.v[0];
         has = true;
 #pragma unroll
         for (int e = 1; e < 4; ++e) acc = pair_exact<F, LUT>(acc, q.v[e], lut);
     }
-    // steps 1..K-1: every lane of a chain that is active here already has a seed
+    // Round k holds vectors k*256 .. k*256+255; chain t takes vector k*256 + t.
+    // Rounds 1 .. Kf-1 are full (every chain has a vector, and a seed from
+    // round 0); round Kf is partial when 256 does not divide nv.  The full
+    // rounds run predicate-free with D rounds of loads in flight per chain.
+    const int64_t Kf = nv / 256;
+    const In* p = vbase + 4 * (int64_t)t;  // chain t's vector in round 0
+    constexpr int64_t kRound = 4 * 256;    // elements per round
     {
         Q4 buf[D];
 #pragma unroll
-        for (int d = 0; d < D; ++d) {
-            const int64_t i = (int64_t)(1 + d) * 256 + t;
-            if (1 + d < K && i < nv) buf[d] = load_vec<KIND>(vbase, i);
-        }
-        for (int64_t k0 = 1; k0 < K; k0 += D) {
+        for (int d = 0; d < D; ++d)
+            if (1 + d < Kf) buf[d] = load_vec_at<KIND>(p + (1 + d) * kRound);
+        int64_t k = 1;
+        for (; k + 2 * D <= Kf; k += D) {  // every load of the block is a full round
 #pragma unroll
             for (int d = 0; d < D; ++d) {
-                const int64_t k = k0 + d;
-                if (k < K) {
+                const Q4 cur = buf[d];
+                buf[d] = load_vec_at<KIND>(p + (k + d + D) * kRound);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc = pair_exact<F, LUT>(acc, cur.v[e], lut);
+            }
+        }
+        for (; k < Kf; k += D) {  // the last (< 2D) full rounds
+#pragma unroll
+            for (int d = 0; d < D; ++d) {
+                if (k + d < Kf) {
                     const Q4 cur = buf[d];
-                    const int64_t in = (k + D) * 256 + t;
-                    if (k + D < K && in < nv) buf[d] = load_vec<KIND>(vbase, in);
-                    const bool active = k * 256 + t < nv;
-                    if constexpr (kSkip) {
+                    if (k + d + D < Kf) buf[d] = load_vec_at<KIND>(p + (k + d + D) * kRound);
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) pair_warp<F, LUT>(acc, cur.v[e], active, lut);
-                    } else if (active) {
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) acc = pair_exact<F, LUT>(acc, cur.v[e], lut);
-                    }
+                    for (int e = 0; e < 4; ++e) acc = pair_exact<F, LUT>(acc, cur.v[e], lut);
                 }
             }
         }
+    }
+    if (Kf >= 1 && Kf * 256 + t < nv) {  // partial round (round 0 was handled above)
+        const Q4 cur = load_vec_at<KIND>(p + Kf * kRound);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc = pair_exact<F, LUT>(acc, cur.v[e], lut);
     }
     if (tail0 + t < N) {
         const int q = IK<KIND>::load1(rowp + tail0 + t);

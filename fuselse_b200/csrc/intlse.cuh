@@ -105,19 +105,4 @@ __device__ __forceinline__ int pair_exact(int a, int b, LaneLut lut) {
     return (int)r;
 }
 
-// Exact pair for a converged warp: the table read is skipped when no lane of
-// the warp can need a non-zero entry (s <= 6).  `active` lanes update `a`.
-template <int F, bool LUT>
-__device__ __forceinline__ void pair_warp(int& a, int b, bool active, LaneLut lut) {
-    uint32_t M, s;
-    uint32_t r = pair_core<F>(a, b, M, s);
-    if constexpr (LUT) {
-        const bool need = active && s < 7u;
-        if (__any_sync(0xffffffffu, need)) {
-            if (need) r += (uint32_t)lut[lut_index<F>(M)];
-        }
-    }
-    if (active) a = (int)r;
-}
-
 }  // namespace fl

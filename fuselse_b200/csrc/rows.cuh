@@ -110,7 +110,8 @@ __device__ __forceinline__ void ms_fold(float& m, float& s, const float* v) {
     float a1 = 0.0f;
     auto e = [&](int i) {
         const float t = fmaf(v[i], kLog2e, -Ml);
-        return (POLY > 0 && i % POLY == POLY - 1) ? ex2_poly(t) : ex2(t);
+        constexpr int P = POLY > 0 ? POLY : 1;
+        return (POLY > 0 && i % P == P - 1) ? ex2_poly(t) : ex2(t);
     };
 #pragma unroll
     for (int i = 0; i < K; i += 2) {
