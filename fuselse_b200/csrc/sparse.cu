@@ -12,12 +12,13 @@
 //   * persistent grid (a few CTAs per SM); each CTA owns a contiguous range of
 //     output nodes and stages their child ids (int32) and log-weights in
 //     shared memory once;
-//   * the batch is walked in tiles of 64 columns, all CTAs on the same tile at
-//     about the same time, so the 64-column slice of element_mars the gathers
-//     touch (rows x 256 B) stays resident in the 126 MB L2 while every child is
-//     gathered by its ~E*nodes/rows parents;
+//   * the batch is walked in column tiles (kTileCols), all CTAs on the same
+//     tile at about the same time, so the gathers of one tile touch one slice
+//     of element_mars while every child is gathered by its ~E*nodes/rows
+//     parents; gathers carry an L2 evict-last policy and the outputs are
+//     stored evict-first, so the slice, not the output stream, holds the L2;
 //   * each thread owns one node x 4 adjacent columns (16-byte gathers), 8
-//     gathers in flight;
+//     gathers in flight, full groups of 8 edges without predicates;
 //   * fp32: online (max, sum-exp) with one EX2 per logit; Q16.16: the
 //     reference's per-edge chain order (edge e feeds chain e mod ET, chains
 //     merged by the ET-lane butterfly) evaluated inside one thread.
@@ -32,11 +33,11 @@ namespace {
 constexpr int kThreads = 256;
 // Batch columns per tile: the tile's slice of element_mars (rows x cols x 4 B)
 // is what L2 should hold while every parent gathers from it; wider tiles also
-// make each gathered child chunk longer (cols x 4 B contiguous), and on B200
-// the 256-byte chunks of 64-column tiles measured fastest (16: 1.31 ms,
-// 32: 0.70 ms, 64: 0.53 ms for the fp32 layer at P=262144, S=65536, E=32).
+// make each gathered child chunk longer (cols x 4 B contiguous).  On B200 the
+// chunk length wins: fp32 layer at P=262144, S=65536, E=32, batch 512 took
+// 1.31 / 0.70 / 0.50 / 0.497 ms with 16 / 32 / 64 / 128-column tiles.
 #ifndef FL_SPARSE_TILE
-#define FL_SPARSE_TILE 64
+#define FL_SPARSE_TILE 128
 #endif
 constexpr int kTileCols = FL_SPARSE_TILE;
 constexpr int kGroup = 8;                       // gathers in flight per thread
@@ -54,18 +55,31 @@ inline int edge_threads(int64_t E) {
     return 8;
 }
 
+// Gathers from element_mars carry an L2 evict-last policy: the tile's slice is
+// re-read by ~E*S/P parents and should outlive the streaming output writes.
+__device__ __forceinline__ uint64_t evict_last_policy() {
+    uint64_t p;
+    asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
 template <int VEC>
 struct ColVec;
 template <>
 struct ColVec<4> {
-    __device__ __forceinline__ static void load(const float* p, float* v) {
-        const float4 r = __ldg(reinterpret_cast<const float4*>(p));
-        v[0] = r.x; v[1] = r.y; v[2] = r.z; v[3] = r.w;
+    __device__ __forceinline__ static void load(const float* p, float* v, uint64_t policy) {
+        asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.f32 {%0,%1,%2,%3}, [%4], %5;"
+                     : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3])
+                     : "l"(p), "l"(policy));
     }
 };
 template <>
 struct ColVec<1> {
-    __device__ __forceinline__ static void load(const float* p, float* v) { v[0] = __ldg(p); }
+    __device__ __forceinline__ static void load(const float* p, float* v, uint64_t policy) {
+        asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.f32 %0, [%1], %2;"
+                     : "=f"(v[0])
+                     : "l"(p), "l"(policy));
+    }
 };
 
 // Per-thread accumulator for VEC columns.
@@ -201,6 +215,7 @@ __global__ void __launch_bounds__(kThreads) sparse_kernel(SparseArgs A) {
     }
     __syncthreads();
     const LaneLut lut{lut_s + (threadIdx.x & 31)};
+    const uint64_t policy = evict_last_policy();
 
     const int sub = threadIdx.x % TPN;
     const int lnode = threadIdx.x / TPN;
@@ -224,13 +239,13 @@ __global__ void __launch_bounds__(kThreads) sparse_kernel(SparseArgs A) {
             const float* wp = s_lw + (size_t)ln * E;
             Acc<Q16, VEC, ET> acc;
             acc.init();
-            for (int e0 = 0; e0 < E; e0 += kGroup) {
-                const int nvalid = min(kGroup, E - e0);
+            // one group of kGroup edges; nvalid < kGroup only for the tail group
+            auto group = [&](int e0, int nvalid) {
                 float lg[kGroup][VEC];
 #pragma unroll
                 for (int g = 0; g < kGroup; ++g) {
                     if (g < nvalid) {
-                        ColVec<VEC>::load(A.em + (int64_t)cp[e0 + g] * A.batch + b0, lg[g]);
+                        ColVec<VEC>::load(A.em + (int64_t)cp[e0 + g] * A.batch + b0, lg[g], policy);
                     } else {
 #pragma unroll
                         for (int c = 0; c < VEC; ++c) lg[g][c] = -INFINITY;
@@ -243,11 +258,14 @@ __global__ void __launch_bounds__(kThreads) sparse_kernel(SparseArgs A) {
                     for (int c = 0; c < VEC; ++c) lg[g][c] += w;
                 }
                 acc.fold(lg, e0, nvalid, lut);
-            }
+            };
+            int e0 = 0;
+            for (; e0 + kGroup <= E; e0 += kGroup) group(e0, kGroup);  // predicate-free
+            if (e0 < E) group(e0, E - e0);
             if (VEC == 4) {
                 float4 o = make_float4(acc.result(0, lut), acc.result(VEC > 1 ? 1 : 0, lut),
                                        acc.result(VEC > 2 ? 2 : 0, lut), acc.result(VEC > 3 ? 3 : 0, lut));
-                *reinterpret_cast<float4*>(outp) = o;
+                st_stream_f4(outp, o);  // written once: evict-first, keep L2 for the gathers
             } else {
                 outp[0] = acc.result(0, lut);
             }
