@@ -38,6 +38,16 @@ enum Kind { kQ16F32 = 0, kQ16I32 = 1, kQ106I16 = 2 };
 #ifndef FL_INTLSE_DLONG
 #define FL_INTLSE_DLONG 24
 #endif
+// Rows whose chains fill the GPU (B*256 >= FILL_WARPS*32*SMs) use one CTA per
+// row and DMID rounds in flight (measured for fp32-input Q16.16 at
+// (512, 128256): 4 -> 60.6 us, 8 -> 72.4 us, 16 -> 78.6 us; the scarce-row
+// shape gave 99.4 us).
+#ifndef FL_INTLSE_FILL_WARPS
+#define FL_INTLSE_FILL_WARPS 8
+#endif
+#ifndef FL_INTLSE_DMID
+#define FL_INTLSE_DMID 4
+#endif
 
 // Reference constants (lse_kernel.cu:23-27): CONV = LOG2_E * 2^16 and
 // LN_2 / 2^16 from the same decimal literals, so the float values match.
@@ -272,18 +282,25 @@ int launch_intlse(const typename IK<KIND>::In* x, float* out, int64_t B, int64_t
                (long long)N);
     if (B == 0) return FL_OK;
     if (int st = bind_device(stream, out)) return st;
-    // spread a row's 256 chains over up to 8 CTAs when rows are scarce
     const int64_t sms = sm_count();
-    int C = 1;
-    while (C < 8 && B * C < 4 * sms) C *= 2;
-    FL_REQUIRE(B * C <= (int64_t)INT32_MAX, "%s: B=%lld too large", what, (long long)B);
-    const int64_t K = (N / 4 + 255) / 256;
+    const int64_t K = (N / 4 + 255) / 256;  // rounds per row
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    // vectors each chain keeps in flight: deeper for long rows, whose few chains
-    // must cover the whole memory latency by themselves
-    int st = K > 64  ? launch_d<KIND, LUT, FL_INTLSE_DLONG>(x, out, B, N, C, s)
+    int st;
+    if (B * 256 >= FL_INTLSE_FILL_WARPS * 32 * sms) {
+        // chains enough to give every SM FL_INTLSE_FILL_WARPS warps: one
+        // 256-thread CTA per row, few rounds in flight (registers for occupancy)
+        st = K > 8 ? launch_d<KIND, LUT, FL_INTLSE_DMID>(x, out, B, N, 1, s)
+                   : launch_d<KIND, LUT, 4>(x, out, B, N, 1, s);
+    } else {
+        // scarce rows: a row's 256 chains spread over up to 8 CTAs, and each
+        // chain keeps many rounds in flight to cover memory latency alone
+        int C = 1;
+        while (C < 8 && B * C < 4 * sms) C *= 2;
+        FL_REQUIRE(B * C <= (int64_t)INT32_MAX, "%s: B=%lld too large", what, (long long)B);
+        st = K > 64  ? launch_d<KIND, LUT, FL_INTLSE_DLONG>(x, out, B, N, C, s)
              : K > 8 ? launch_d<KIND, LUT, 16>(x, out, B, N, C, s)
                      : launch_d<KIND, LUT, 4>(x, out, B, N, C, s);
+    }
     if (st) return st;
     return check_launch(what);
 }
