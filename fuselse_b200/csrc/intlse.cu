@@ -147,7 +147,7 @@ __global__ void __launch_bounds__(CTA) intlse_rows_kernel(
         fill_lane_lut<CTA>(lut_s, F == 16 ? kLutQ16 : kLutQ10_6);
         __syncthreads();
     }
-    const LaneLut lut{lut_s + lane};
+    const LaneLut lut{lut_s, lane};
 
     const In* rowp = x + row * N;
     const int64_t head = head_count<KIND>(rowp, N);

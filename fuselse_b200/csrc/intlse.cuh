@@ -47,17 +47,26 @@ __device__ __forceinline__ uint32_t shr_u32(uint32_t v, uint32_t s) {
 
 // Per-lane replicated copy of a 64-entry table in shared memory: entry i of
 // lane l lives at word i*32 + l, so 32 lanes reading 32 different entries hit
-// 32 different banks.
+// 32 different banks.  The byte offset of (i, l) is i*128 | l*4 (disjoint
+// bits), so a lookup from the pair's M is one shift and one three-input
+// logic op; the table's own shared address is a link-time constant that
+// folds into the load's offset.
 // Reads go through an explicit shared-window address (ld.shared): a generic
 // pointer kept in a struct can compile to generic loads, which take the
 // longer global-memory path.
 struct LaneLut {
-    uint32_t base;  // shared-window byte address of this lane's column
-    __device__ __forceinline__ explicit LaneLut(const int* lane_column)
-        : base(static_cast<uint32_t>(__cvta_generic_to_shared(lane_column))) {}
-    __device__ __forceinline__ int operator[](uint32_t i) const {
+    uint32_t table;  // shared-window byte address of the table
+    uint32_t lane4;  // this lane's column, in bytes
+    __device__ __forceinline__ LaneLut(const int* table_s, int lane)
+        : table(static_cast<uint32_t>(__cvta_generic_to_shared(table_s))),
+          lane4(static_cast<uint32_t>(lane) * 4u) {}
+    // Correction entry for the pair's M: index (M >> 10) & 63 for Q16.16,
+    // M & 63 for Q10.6.
+    template <int F>
+    __device__ __forceinline__ int at(uint32_t M) const {
+        const uint32_t off = (F == 16 ? (M >> 3) : (M << 7)) & (63u << 7);
         int v;  // volatile: stays after the __syncthreads() that publishes the table
-        asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(base + i * 128u));
+        asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(table + (off | lane4)));
         return v;
     }
 };
@@ -68,15 +77,6 @@ __device__ __forceinline__ void fill_lane_lut(int* dst, const int* src) {
     for (int i = threadIdx.x; i < 64 * 32 / 4; i += THREADS) {
         const int v = src[i >> 3];
         reinterpret_cast<int4*>(dst)[i] = make_int4(v, v, v, v);
-    }
-}
-
-template <int F>
-__device__ __forceinline__ uint32_t lut_index(uint32_t M) {
-    if constexpr (F == 16) {
-        return (M >> 10) & 63u;
-    } else {
-        return M & 63u;
     }
 }
 
@@ -101,7 +101,7 @@ template <int F, bool LUT>
 __device__ __forceinline__ int pair_exact(int a, int b, LaneLut lut) {
     uint32_t M, s;
     uint32_t r = pair_core<F>(a, b, M, s);
-    if constexpr (LUT) r += (uint32_t)lut[lut_index<F>(M)];
+    if constexpr (LUT) r += (uint32_t)lut.at<F>(M);
     return (int)r;
 }
 

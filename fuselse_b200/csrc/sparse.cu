@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(kThreads) sparse_kernel(SparseArgs A) {
         if (bad && s_row[ln] >= 0) s_row[ln] |= (1LL << 62);
     }
     __syncthreads();
-    const LaneLut lut{lut_s + (threadIdx.x & 31)};
+    const LaneLut lut{lut_s, (int)(threadIdx.x & 31)};
     const uint64_t policy = evict_last_policy();
 
     const int sub = threadIdx.x % TPN;

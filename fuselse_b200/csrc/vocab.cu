@@ -5,20 +5,24 @@
 //   kernel 1 (vocab_scatter_kernel): one warp per row folds the local columns
 //     into (m, s) = (max, sum exp(x - m)) and stores the pair straight into
 //     every rank's exchange buffer (P2P stores through the peer mappings of a
-//     symmetric allocation); the last of its CTAs fences at system scope and
-//     adds 1 to this rank's counter in every rank's flag array (release,
-//     system scope), so a counter equals the number of calls delivered;
-//   kernel 2 (vocab_combine_kernel, one thread per row): every CTA waits until
-//     every rank's counter shows this call's contributions (acquire, system
+//     symmetric allocation).  It has no epilogue: no fence, no counter.
+//   kernel 2 (vocab_combine_kernel, one thread per row): every CTA first
+//     publishes — threads 0..G-1 store the call's epoch into this rank's flag
+//     word of every rank's buffer (release, system scope).  Kernel 1 finished
+//     before kernel 2 started (stream order), so the release covers every pair
+//     this rank delivered; the store is idempotent (every CTA stores the same
+//     epoch), so no CTA depends on another having been scheduled.  Then every
+//     CTA waits until every rank's flag shows this call (acquire, system
 //     scope; bounded by an iteration cap and a 2 s clock limit, after which it
-//     writes NaN rows and sets a sticky error word), merges the G pairs of each
-//     row and finishes lse = M + log(sum_g s_g exp(m_g - M)); the last CTA to
-//     finish advances the call epoch.
+//     writes NaN rows and sets a sticky error word), merges the G pairs of
+//     each row and finishes lse = M + log(sum_g s_g exp(m_g - M)); the last
+//     CTA to finish advances the call epoch.
 // The epoch lives in the buffer, so captured CUDA graphs replay correctly;
-// pairs alternate between two slots by epoch parity, so a rank that starts the
-// next call cannot overwrite pairs another rank is still reading (it can only
-// get one call ahead).  Every rank must make the same sequence of calls with
-// the same B.
+// pairs alternate between two slots by epoch parity.  A rank's flag reaches
+// epoch k only once that rank has finished call k-1 entirely, so a rank that
+// runs ahead can write the other slot at most: it cannot overwrite pairs
+// another rank is still reading.  Every rank must make the same sequence of
+// calls with the same B.
 //
 // Exchange buffer layout (identical on all ranks, 256-byte aligned):
 //   [0, 256)                 header: finished epoch, sticky error, epoch in
@@ -51,14 +55,14 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     return v;
 }
 
-__device__ __forceinline__ void red_release_sys_add(uint32_t* p, uint32_t v) {
-    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 // Header words (local use): [0] epoch of the last finished call, [1] sticky
 // error, [2] epoch of the call in flight (written by the scatter kernel, read
-// by every combine CTA), [3] combine CTAs finished and [4] scatter CTAs
-// finished in the call in flight (both reset by the last CTA).
+// by every combine CTA), [3] combine CTAs finished in the call in flight
+// (reset by the last CTA).
 template <typename T>
 __global__ void __launch_bounds__(kRowsPerCta * 32) vocab_scatter_kernel(
     const T* __restrict__ x, int64_t B, int64_t N, unsigned char* const* __restrict__ peers,
@@ -69,35 +73,14 @@ __global__ void __launch_bounds__(kRowsPerCta * 32) vocab_scatter_kernel(
     const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(header) + 1;
     const int64_t slot = epoch & 1u;
     if (blockIdx.x == 0 && threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(header + 2) = epoch;
-    if (row < B) {
-        float m, s;
-        fold_row_warp(x + row * N, N, lane, m, s);
-        // lanes 0..G-1 each deliver the pair to one rank
-        for (int p = lane; p < G; p += 32) {
-            float2* dst = reinterpret_cast<float2*>(peers[p] + pairs_offset(G)) +
-                          ((slot * G + rank) * B + row);
-            *dst = make_float2(m, s);
-        }
-    }
-    // Publication, one system-scope fence per call: the barrier orders this
-    // CTA's stores before thread 0's GPU-scope release (fence + count); the
-    // last CTA to count has observed every CTA's release, so its system-scope
-    // fence — cumulative — orders all of the call's stores before the
-    // release adds that tell the peers this rank's pairs are in place.
-    __shared__ int last;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        last = atomicAdd(header + 4, 1u) == gridDim.x - 1;
-        if (last) {
-            header[4] = 0;
-            __threadfence_system();
-        }
-    }
-    __syncthreads();
-    if (last && threadIdx.x < G) {
-        uint32_t* flags = reinterpret_cast<uint32_t*>(peers[threadIdx.x] + kHeaderBytes);
-        red_release_sys_add(flags + rank, 1u);
+    if (row >= B) return;
+    float m, s;
+    fold_row_warp(x + row * N, N, lane, m, s);
+    // lanes 0..G-1 each deliver the pair to one rank
+    for (int p = lane; p < G; p += 32) {
+        float2* dst = reinterpret_cast<float2*>(peers[p] + pairs_offset(G)) +
+                      ((slot * G + rank) * B + row);
+        *dst = make_float2(m, s);
     }
 }
 
@@ -105,21 +88,26 @@ constexpr int kCombineThreads = 256;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 constexpr uint32_t kWaitLimitIters = 1u << 26;
 
-// One thread per row; every CTA waits for the flags itself.  The last CTA to
-// finish advances the finished-call epoch.
+// One thread per row; every CTA publishes this rank's delivery, then waits
+// for the flags itself.  The last CTA to finish advances the finished-call
+// epoch.
 __global__ void __launch_bounds__(kCombineThreads) vocab_combine_kernel(
-    unsigned char* __restrict__ local, float* __restrict__ out, int64_t B, int G, uint32_t ngroups) {
+    unsigned char* const* __restrict__ peers, unsigned char* __restrict__ local,
+    float* __restrict__ out, int64_t B, int rank, int G) {
     __shared__ int timed_out;
     uint32_t* header = reinterpret_cast<uint32_t*>(local);
     const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(header + 2);
-    const uint32_t expected = epoch;  // every rank adds 1 per call
     if (threadIdx.x == 0) timed_out = 0;
+    for (int q = threadIdx.x; q < G; q += kCombineThreads) {
+        __threadfence_system();
+        st_release_sys(reinterpret_cast<uint32_t*>(peers[q] + kHeaderBytes) + rank, epoch);
+    }
     __syncthreads();
-    if (threadIdx.x < G) {
-        const uint32_t* flag = reinterpret_cast<const uint32_t*>(local + kHeaderBytes) + threadIdx.x;
+    for (int q = threadIdx.x; q < G; q += kCombineThreads) {
+        const uint32_t* flag = reinterpret_cast<const uint32_t*>(local + kHeaderBytes) + q;
         const uint64_t t0 = global_ns();
         for (uint32_t it = 0;; ++it) {
-            if ((int32_t)(ld_acquire_sys(flag) - expected) >= 0) break;
+            if ((int32_t)(ld_acquire_sys(flag) - epoch) >= 0) break;
             if (it >= kWaitLimitIters || global_ns() - t0 > kWaitLimitNs) {
                 atomicExch(&timed_out, 1);
                 break;
@@ -194,8 +182,7 @@ extern "C" int fl_lse_vocab_exchange(const void* x, int dtype, int64_t B, int64_
             reinterpret_cast<const __half*>(x), B, N, peers, local, rank, G);
     if (int st = check_launch(what)) return st;
     const int64_t cgrid = (B + kCombineThreads - 1) / kCombineThreads;
-    vocab_combine_kernel<<<(unsigned)cgrid, kCombineThreads, 0, s>>>(local, out, B, G,
-                                                                     (uint32_t)ngroups);
+    vocab_combine_kernel<<<(unsigned)cgrid, kCombineThreads, 0, s>>>(peers, local, out, B, rank, G);
     return check_launch(what);
 }
 
@@ -278,7 +265,6 @@ extern "C" int fl_lse_vocab_exchange_noalloc(const void* x, int dtype, int64_t B
             reinterpret_cast<const __half*>(x), B, N, d.peers, d.exchange, 0, 1);
     if (int st = check_launch(what)) return st;
     const int64_t cgrid = (B + kCombineThreads - 1) / kCombineThreads;
-    vocab_combine_kernel<<<(unsigned)cgrid, kCombineThreads, 0, s>>>(d.exchange, out, B, 1,
-                                                                     (uint32_t)ngroups);
+    vocab_combine_kernel<<<(unsigned)cgrid, kCombineThreads, 0, s>>>(d.peers, d.exchange, out, B, 0, 1);
     return check_launch(what);
 }
