@@ -1,7 +1,7 @@
 """Benchmark of the row log-sum-exp hot path on B200 (driver contract).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload fwdbwd_f32|fwd_f32|f16_vocab|intlse_q16|intlse_q10_6|sparse_f32|sparse_q16]
+                    [--workload fwdbwd_f32|fwd_f32|sls_f32|f16_vocab|intlse_q16|intlse_q10_6|sparse_f32|sparse_q16]
 
 One JSON line on rank 0.  Default workload (the headline, BASELINE metric):
 FuseLSE fp32 forward + backward over (B, N) = (512, 128256), x ~ N(0, 1),
@@ -190,6 +190,43 @@ class FwdBwdF32(Workload):
         self.gx_host.copy_(x.grad, non_blocking=True)
 
 
+class SelectiveF32(Workload):
+    """Fused selective log-softmax forward + backward over RLHF-shaped logits
+    (the Llama-3 configuration of run_rlhf.py: batch 4, T-1 = 1023 positions,
+    V = 128256), targets uniform over the vocabulary, upstream gradient ones."""
+    name = "sls_f32"
+    dtype = "f32"
+
+    def __init__(self, dev, seed, batch=4, T=1023, V=128256):
+        from fuselse_b200 import ext, workloads as W
+        self.ext = ext
+        self.R, self.V = batch * T, V
+        self.x = W.fp32_rows(self.R, V, seed, dev)
+        gen = torch.Generator(device="cpu").manual_seed(seed + 7)
+        self.t = torch.randint(0, V, (self.R,), generator=gen).to(dev)
+        self.g = torch.ones(self.R, device=dev)
+        self.config = {"workload": f"selective log-softmax fp32 forward+backward, logits ({batch},{T},{V}) "
+                                   "x~N(0,1), targets uniform, grad ones",
+                       "rows": self.R, "V": V,
+                       "l2": "inputs larger than L2 (logits 2.1 GB), steps back to back",
+                       "parallelism": "batch rows, one process per GPU, no collective"}
+        self.launches_per_step = 2
+
+    def _fwd(self):
+        self.logp, self.lse = self.ext.selective_logsoftmax_rows(self.x, self.t)
+
+    def _bwd(self):
+        self.gx = self.ext.selective_logsoftmax_backward(self.g, self.x, self.lse, self.t)
+
+    def kernels(self):
+        R, V = self.R, self.V
+        return [("sls_fwd", self._fwd, R * V * 4 + R * (8 + 4 + 4)),
+                ("sls_bwd", self._bwd, 2 * R * V * 4 + R * (4 + 4 + 8))]
+
+    def rows(self):
+        return self.R
+
+
 class F16Vocab(Workload):
     name = "f16_vocab"
     dtype = "f16"
@@ -239,7 +276,7 @@ class IntLSE(Workload):
         self.ext, self.kind = ext, kind
         x, q16, q106 = W.intlse_inputs(B, N, seed, dev)
         self.q = q16 if kind == "q16" else q106
-        self.name = "intlse_" + kind
+        self.name = "intlse_" + kind + ("" if (B, N) == (16384, 4096) else "_long")
         self.dtype = "int32" if kind == "q16" else "int16"
         self.B, self.N = B, N
         self.config = {"workload": f"IntLSE {kind} (B,N)=({B},{N}), x~N(0,2^2)",
@@ -291,6 +328,8 @@ def make_workload(name, dev, seed, world, rank):
         return FwdBwdF32(dev, seed)
     if name == "fwd_f32":
         return FwdBwdF32(dev, seed, do_bwd=False)
+    if name == "sls_f32":
+        return SelectiveF32(dev, seed)
     if name == "f16_vocab":
         return F16Vocab(dev, seed, world, rank)
     if name == "f16_vocab_nccl":

@@ -10,9 +10,12 @@ A drop-in for the FuseLSE / IntLSE reference call surface:
 (onepass_lse_float[_robust|_backward], batched_logsumexp[_nolut|_fp16|_q10_6],
 sparse_forward_float, sparse_forward_q16) backed by the C ABI of
 libfuselse_b200.so (include/fuselse_b200.h).  `fuselse_b200.distributed`
-shards rows across GPUs and combines vocab-sharded rows over NCCL.
+shards rows across GPUs and combines vocab-sharded rows over NCCL or the
+library's own NVLink exchange.  `selective_log_softmax(logits, index)` is the
+fused per-token log-probability (target gather + LSE in one pass).
 """
 from . import ext
 from .autograd import make_fuselse_logsumexp
+from .selective import selective_log_softmax
 
-__all__ = ["ext", "make_fuselse_logsumexp"]
+__all__ = ["ext", "make_fuselse_logsumexp", "selective_log_softmax"]

@@ -28,12 +28,56 @@ namespace cg = cooperative_groups;
 namespace fl {
 namespace {
 
+// What a row reduction writes.
+enum OutMode {
+    kOutLse = 0,      // out[row] = lse
+    kOutPartial = 1,  // out[row] = (m, s) as a float2
+    kOutSelect = 2,   // out[row] = lse, sel.logp[row] = x[row, index[row]] - lse
+};
+
+// Selective log-softmax outputs (kOutSelect only).  An index outside [0, N)
+// gives a NaN log-probability and sets *err (when err is not NULL).
+struct SelArgs {
+    const int64_t* index;
+    float* logp;
+    int* err;
+};
+
+// Thread that finishes a row: fetch the target logit early (its load overlaps
+// the row's stream) and write lse and x[t] - lse at the end.
+template <typename T>
+struct Target {
+    float xt = 0.0f;
+    bool bad = false;
+    __device__ __forceinline__ void fetch(const T* rowp, int64_t N, int64_t row, const SelArgs& sel) {
+        const int64_t t = __ldg(sel.index + row);
+        bad = !(t >= 0 && t < N);
+        xt = bad ? 0.0f : Elem<T>::load1(rowp + t);
+    }
+    __device__ __forceinline__ void finish(float lse, int64_t row, const SelArgs& sel) const {
+        sel.logp[row] = bad ? __int_as_float(0x7fc00000) : xt - lse;
+        if (bad && sel.err) atomicOr(sel.err, 1);
+    }
+};
+
+template <typename T, int MODE>
+__device__ __forceinline__ void write_row(float* out, int64_t row, float m, float s,
+                                          float empty_value, const Target<T>& tg,
+                                          const SelArgs& sel) {
+    if (MODE == kOutPartial) {
+        reinterpret_cast<float2*>(out)[row] = make_float2(m, s);
+    } else {
+        const float lse = ms_finalize(m, s, empty_value);
+        out[row] = lse;
+        if (MODE == kOutSelect) tg.finish(lse, row, sel);
+    }
+}
+
 // One CTA per row segment; the nseg CTAs of a row form one cluster.
-// PARTIAL: write (m, s) pairs instead of the finished value.
-template <typename T, bool PARTIAL>
+template <typename T, int MODE>
 __global__ void __launch_bounds__(FwdShape<T>::kThreads) lse_segment_kernel(
     const T* __restrict__ x, float* __restrict__ out, int64_t B, int64_t N,
-    int nseg, float empty_value) {
+    int nseg, float empty_value, SelArgs sel) {
     constexpr int E = Elem<T>::kPerVec;
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = static_cast<int>(blockIdx.x % nseg);
@@ -41,8 +85,10 @@ __global__ void __launch_bounds__(FwdShape<T>::kThreads) lse_segment_kernel(
     __shared__ float2 seg_part[kMaxSeg];
 
     float m = -INFINITY, s = 0.0f;
+    Target<T> tg;
     if (row < B) {
         const T* rowp = x + row * N;
+        if (MODE == kOutSelect && rank == 0 && threadIdx.x == 0) tg.fetch(rowp, N, row, sel);
         const int64_t head = head_elems(rowp, N);
         const int64_t nv = (N - head) / E;
         const int64_t tail0 = head + nv * E;
@@ -70,32 +116,22 @@ __global__ void __launch_bounds__(FwdShape<T>::kThreads) lse_segment_kernel(
             for (int r = 1; r < nseg; ++r) ms_merge(m, s, seg_part[r].x, seg_part[r].y);
         }
     }
-    if (threadIdx.x == 0 && row < B) {
-        if (PARTIAL) {
-            reinterpret_cast<float2*>(out)[row] = make_float2(m, s);
-        } else {
-            out[row] = ms_finalize(m, s, empty_value);
-        }
-    }
+    if (threadIdx.x == 0 && row < B) write_row<T, MODE>(out, row, m, s, empty_value, tg, sel);
 }
 
 // One warp per row for short rows.
-template <typename T, bool PARTIAL>
+template <typename T, int MODE>
 __global__ void __launch_bounds__(kThreads) lse_warp_kernel(
     const T* __restrict__ x, float* __restrict__ out, int64_t B, int64_t N,
-    float empty_value) {
+    float empty_value, SelArgs sel) {
     const int lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
     if (row >= B) return;
+    Target<T> tg;
+    if (MODE == kOutSelect && lane == 0) tg.fetch(x + row * N, N, row, sel);
     float m, s;
     fold_row_warp(x + row * N, N, lane, m, s);
-    if (lane == 0) {
-        if (PARTIAL) {
-            reinterpret_cast<float2*>(out)[row] = make_float2(m, s);
-        } else {
-            out[row] = ms_finalize(m, s, empty_value);
-        }
-    }
+    if (lane == 0) write_row<T, MODE>(out, row, m, s, empty_value, tg, sel);
 }
 
 __global__ void lse_combine_kernel(const float2* __restrict__ ms, float* __restrict__ out,
@@ -111,59 +147,81 @@ __global__ void lse_combine_kernel(const float2* __restrict__ ms, float* __restr
 }
 
 // gx = g[row] * exp(x - lse[row]) over chunks of one row.
+// SEL (selective log-softmax backward): gx = g[row] * ([j == index[row]] - exp(x - lse[row])),
+// the one-hot term added by the thread that owns column index[row].
 constexpr int kBwdUnroll = 4;
 
+template <bool SEL>
 __global__ void __launch_bounds__(kThreads) lse_bwd_kernel(
     const float* __restrict__ g, const float* __restrict__ x,
     const float* __restrict__ lse, float* __restrict__ gx, int64_t B, int64_t N,
-    int nchunk, int64_t chunk_vec) {
+    int nchunk, int64_t chunk_vec, const int64_t* __restrict__ index) {
     const int chunk = static_cast<int>(blockIdx.x % nchunk);
     const int64_t row = static_cast<int64_t>(blockIdx.x / nchunk);
     const float* xr = x + row * N;
     float* gr = gx + row * N;
-    const float gs = __ldg(g + row);
+    const float g0 = __ldg(g + row);
+    const float gs = SEL ? -g0 : g0;
     const float ll = __ldg(lse + row) * kLog2e;
     const int64_t head = head_elems(xr, N);
     const int64_t nv = (N - head) / 4;
     const int64_t tail0 = head + nv * 4;
     const int64_t v0 = min(nv, chunk * chunk_vec), v1 = min(nv, v0 + chunk_vec);
+    // target column relative to the first vector (any value when !SEL)
+    const int64_t tv = SEL ? __ldg(index + row) - head : -1;
     const uint4* xv = reinterpret_cast<const uint4*>(xr + head);
     float4* gv = reinterpret_cast<float4*>(gr + head);
     auto op = [&](float v) { return gs * ex2(fmaf(v, kLog2e, -ll)); };
+    auto vec = [&](uint4 r, int64_t i) {
+        float4 o = make_float4(op(__uint_as_float(r.x)), op(__uint_as_float(r.y)),
+                               op(__uint_as_float(r.z)), op(__uint_as_float(r.w)));
+        if (SEL) {
+            const uint64_t d = static_cast<uint64_t>(tv - 4 * i);
+            if (d < 4) {
+                if (d == 0) o.x += g0;
+                else if (d == 1) o.y += g0;
+                else if (d == 2) o.z += g0;
+                else o.w += g0;
+            }
+        }
+        return o;
+    };
+    auto one = [&](int64_t j) {  // scalar column j of the row
+        float o = op(__ldg(xr + j));
+        if (SEL && j == tv + head) o += g0;
+        gr[j] = o;
+    };
     int64_t i = v0 + threadIdx.x;
     for (; i + (kBwdUnroll - 1) * kThreads < v1; i += kBwdUnroll * kThreads) {
         uint4 r[kBwdUnroll];
 #pragma unroll
         for (int u = 0; u < kBwdUnroll; ++u) r[u] = ld_stream_u4(xv + i + u * kThreads);
 #pragma unroll
-        for (int u = 0; u < kBwdUnroll; ++u) {
-            float4 o = make_float4(op(__uint_as_float(r[u].x)), op(__uint_as_float(r[u].y)),
-                                   op(__uint_as_float(r[u].z)), op(__uint_as_float(r[u].w)));
-            st_stream_f4(gv + i + u * kThreads, o);
-        }
+        for (int u = 0; u < kBwdUnroll; ++u) st_stream_f4(gv + i + u * kThreads, vec(r[u], i + u * kThreads));
     }
-    for (; i < v1; i += kThreads) {
-        const uint4 r = ld_stream_u4(xv + i);
-        float4 o = make_float4(op(__uint_as_float(r.x)), op(__uint_as_float(r.y)),
-                               op(__uint_as_float(r.z)), op(__uint_as_float(r.w)));
-        st_stream_f4(gv + i, o);
-    }
+    for (; i < v1; i += kThreads) st_stream_f4(gv + i, vec(ld_stream_u4(xv + i), i));
     if (chunk == 0) {
-        if (threadIdx.x < head) gr[threadIdx.x] = op(__ldg(xr + threadIdx.x));
-        if (tail0 + threadIdx.x < N) gr[tail0 + threadIdx.x] = op(__ldg(xr + tail0 + threadIdx.x));
+        if (threadIdx.x < head) one(threadIdx.x);
+        if (tail0 + threadIdx.x < N) one(tail0 + threadIdx.x);
     }
 }
 
 // Element-wise backward for x / gx buffers whose 16-byte phases differ.
+template <bool SEL>
 __global__ void lse_bwd_scalar_kernel(const float* __restrict__ g, const float* __restrict__ x,
                                       const float* __restrict__ lse, float* __restrict__ gx,
-                                      int64_t B, int64_t N) {
+                                      int64_t B, int64_t N, const int64_t* __restrict__ index) {
     const int64_t row = blockIdx.y;
-    const float gs = __ldg(g + row);
+    const float g0 = __ldg(g + row);
+    const float gs = SEL ? -g0 : g0;
     const float ll = __ldg(lse + row) * kLog2e;
+    const int64_t t = SEL ? __ldg(index + row) : -1;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < N;
-         i += (int64_t)gridDim.x * blockDim.x)
-        gx[row * N + i] = gs * ex2(fmaf(__ldg(x + row * N + i), kLog2e, -ll));
+         i += (int64_t)gridDim.x * blockDim.x) {
+        float o = gs * ex2(fmaf(__ldg(x + row * N + i), kLog2e, -ll));
+        if (SEL && i == t) o += g0;
+        gx[row * N + i] = o;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -202,13 +260,13 @@ int choose_nseg(int64_t B, int64_t N) {
     return static_cast<int>(nseg);
 }
 
-template <typename T, bool PARTIAL>
+template <typename T, int MODE>
 int launch_rows(const T* x, float* out, int64_t B, int64_t N, float empty_value,
-                cudaStream_t stream, const char* what) {
+                cudaStream_t stream, const char* what, SelArgs sel = SelArgs{}) {
     if (warp_per_row<T>(B, N)) {
         const int64_t grid = (B + kWarps - 1) / kWarps;
         FL_REQUIRE(grid <= INT32_MAX, "%s: B=%lld too large", what, (long long)B);
-        lse_warp_kernel<T, PARTIAL><<<(unsigned)grid, kThreads, 0, stream>>>(x, out, B, N, empty_value);
+        lse_warp_kernel<T, MODE><<<(unsigned)grid, kThreads, 0, stream>>>(x, out, B, N, empty_value, sel);
         return check_launch(what);
     }
     const int nseg = choose_nseg<T>(B, N);
@@ -226,8 +284,8 @@ int launch_rows(const T* x, float* out, int64_t B, int64_t N, float empty_value,
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    FL_CUDA(cudaLaunchKernelEx(&cfg, lse_segment_kernel<T, PARTIAL>, x, out, B, N, nseg,
-                               empty_value));
+    FL_CUDA(cudaLaunchKernelEx(&cfg, lse_segment_kernel<T, MODE>, x, out, B, N, nseg,
+                               empty_value, sel));
     return check_launch(what);
 }
 
@@ -252,7 +310,7 @@ extern "C" int fl_lse_f32_fwd(const float* x, float* out, int64_t B, int64_t N, 
     if (int st = check_rows<float>(x, out, B, N, "fl_lse_f32_fwd")) return st;
     if (B == 0) return FL_OK;
     if (int st = bind_device(stream, out)) return st;
-    return launch_rows<float, false>(x, out, B, N, robust ? -INFINITY : -1.0e30f,
+    return launch_rows<float, kOutLse>(x, out, B, N, robust ? -INFINITY : -1.0e30f,
                                      reinterpret_cast<cudaStream_t>(stream), "fl_lse_f32_fwd");
 }
 
@@ -262,7 +320,7 @@ extern "C" int fl_lse_f16_fwd(const uint16_t* x, float* out, int64_t B, int64_t 
     if (int st = check_rows<__half>(x, out, B, N, "fl_lse_f16_fwd")) return st;
     if (B == 0) return FL_OK;
     if (int st = bind_device(stream, out)) return st;
-    return launch_rows<__half, false>(reinterpret_cast<const __half*>(x), out, B, N, -1.0e30f,
+    return launch_rows<__half, kOutLse>(reinterpret_cast<const __half*>(x), out, B, N, -1.0e30f,
                                       reinterpret_cast<cudaStream_t>(stream), "fl_lse_f16_fwd");
 }
 
@@ -273,7 +331,7 @@ extern "C" int fl_lse_f32_partial(const float* x, float* ms, int64_t B, int64_t 
     FL_REQUIRE(aligned_to(ms, 8), "fl_lse_f32_partial: ms is not 8-byte aligned");
     if (B == 0) return FL_OK;
     if (int st = bind_device(stream, ms)) return st;
-    return launch_rows<float, true>(x, ms, B, N, -INFINITY, reinterpret_cast<cudaStream_t>(stream),
+    return launch_rows<float, kOutPartial>(x, ms, B, N, -INFINITY, reinterpret_cast<cudaStream_t>(stream),
                                     "fl_lse_f32_partial");
 }
 
@@ -284,7 +342,7 @@ extern "C" int fl_lse_f16_partial(const uint16_t* x, float* ms, int64_t B, int64
     FL_REQUIRE(aligned_to(ms, 8), "fl_lse_f16_partial: ms is not 8-byte aligned");
     if (B == 0) return FL_OK;
     if (int st = bind_device(stream, ms)) return st;
-    return launch_rows<__half, true>(reinterpret_cast<const __half*>(x), ms, B, N, -INFINITY,
+    return launch_rows<__half, kOutPartial>(reinterpret_cast<const __half*>(x), ms, B, N, -INFINITY,
                                      reinterpret_cast<cudaStream_t>(stream), "fl_lse_f16_partial");
 }
 
@@ -304,15 +362,18 @@ extern "C" int fl_lse_combine(const float* ms, float* out, int64_t G, int64_t B,
     return check_launch("fl_lse_combine");
 }
 
-extern "C" int fl_lse_f32_bwd(const float* g, const float* x, const float* lse, float* gx,
-                              int64_t B, int64_t N, fl_stream_t stream) {
-    clear_error();
-    const char* what = "fl_lse_f32_bwd";
+namespace fl {
+namespace {
+
+template <bool SEL>
+int launch_bwd(const float* g, const float* x, const float* lse, const int64_t* index, float* gx,
+               int64_t B, int64_t N, fl_stream_t stream, const char* what) {
     FL_REQUIRE(B >= 0 && N >= 0, "%s: negative shape", what);
     if (B == 0 || N == 0) return FL_OK;
-    FL_REQUIRE(g && x && lse && gx, "%s: NULL buffer", what);
-    FL_REQUIRE(aligned_to(g, 4) && aligned_to(x, 4) && aligned_to(lse, 4) && aligned_to(gx, 4),
-               "%s: buffers must be 4-byte aligned", what);
+    FL_REQUIRE(g && x && lse && gx && (!SEL || index), "%s: NULL buffer", what);
+    FL_REQUIRE(aligned_to(g, 4) && aligned_to(x, 4) && aligned_to(lse, 4) && aligned_to(gx, 4) &&
+                   aligned_to(index, 8),
+               "%s: misaligned buffer", what);
     if (int st = bind_device(stream, gx)) return st;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const bool same_phase = ((reinterpret_cast<uintptr_t>(x) ^ reinterpret_cast<uintptr_t>(gx)) & 15u) == 0;
@@ -320,7 +381,8 @@ extern "C" int fl_lse_f32_bwd(const float* g, const float* x, const float* lse, 
         FL_REQUIRE(B <= 65535, "%s: B=%lld too large for buffers of differing alignment", what,
                    (long long)B);
         const int64_t bx = std::min<int64_t>((N + 255) / 256, 1024);
-        lse_bwd_scalar_kernel<<<dim3((unsigned)bx, (unsigned)B), 256, 0, s>>>(g, x, lse, gx, B, N);
+        lse_bwd_scalar_kernel<SEL><<<dim3((unsigned)bx, (unsigned)B), 256, 0, s>>>(g, x, lse, gx, B, N,
+                                                                                   index);
         return check_launch(what);
     }
     const int64_t nv = N / 4 + 1;
@@ -329,6 +391,54 @@ extern "C" int fl_lse_f32_bwd(const float* g, const float* x, const float* lse, 
     const int64_t nchunk = (nv + chunk_vec - 1) / chunk_vec;
     const int64_t grid = B * nchunk;
     FL_REQUIRE(grid <= INT32_MAX, "%s: B*N too large", what);
-    lse_bwd_kernel<<<(unsigned)grid, kThreads, 0, s>>>(g, x, lse, gx, B, N, (int)nchunk, chunk_vec);
+    lse_bwd_kernel<SEL><<<(unsigned)grid, kThreads, 0, s>>>(g, x, lse, gx, B, N, (int)nchunk,
+                                                            chunk_vec, index);
     return check_launch(what);
+}
+
+template <typename T>
+int launch_select(const T* x, const int64_t* index, float* logp, float* lse, int64_t B, int64_t N,
+                  float empty_value, int* err_flag, fl_stream_t stream, const char* what) {
+    if (int st = check_rows<T>(x, lse, B, N, what)) return st;
+    FL_REQUIRE(B == 0 || (index && logp), "%s: NULL buffer", what);
+    FL_REQUIRE(aligned_to(index, 8) && aligned_to(logp, 4) && aligned_to(err_flag, 4),
+               "%s: misaligned buffer", what);
+    FL_REQUIRE(B == 0 || N > 0, "%s: rows are empty (N = 0): no column to select", what);
+    if (B == 0) return FL_OK;
+    if (int st = bind_device(stream, lse)) return st;
+    return launch_rows<T, kOutSelect>(x, lse, B, N, empty_value,
+                                      reinterpret_cast<cudaStream_t>(stream), what,
+                                      SelArgs{index, logp, err_flag});
+}
+
+}  // namespace
+}  // namespace fl
+
+extern "C" int fl_lse_f32_bwd(const float* g, const float* x, const float* lse, float* gx,
+                              int64_t B, int64_t N, fl_stream_t stream) {
+    clear_error();
+    return launch_bwd<false>(g, x, lse, nullptr, gx, B, N, stream, "fl_lse_f32_bwd");
+}
+
+extern "C" int fl_selective_logsoftmax_f32(const float* x, const int64_t* index, float* logp,
+                                           float* lse, int64_t B, int64_t N, int robust,
+                                           int* err_flag, fl_stream_t stream) {
+    clear_error();
+    return launch_select<float>(x, index, logp, lse, B, N, robust ? -INFINITY : -1.0e30f, err_flag,
+                                stream, "fl_selective_logsoftmax_f32");
+}
+
+extern "C" int fl_selective_logsoftmax_f16(const uint16_t* x, const int64_t* index, float* logp,
+                                           float* lse, int64_t B, int64_t N, int* err_flag,
+                                           fl_stream_t stream) {
+    clear_error();
+    return launch_select<__half>(reinterpret_cast<const __half*>(x), index, logp, lse, B, N,
+                                 -1.0e30f, err_flag, stream, "fl_selective_logsoftmax_f16");
+}
+
+extern "C" int fl_selective_logsoftmax_bwd(const float* g, const float* x, const float* lse,
+                                           const int64_t* index, float* gx, int64_t B, int64_t N,
+                                           fl_stream_t stream) {
+    clear_error();
+    return launch_bwd<true>(g, x, lse, index, gx, B, N, stream, "fl_selective_logsoftmax_bwd");
 }

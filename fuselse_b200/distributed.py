@@ -12,12 +12,16 @@ Two layouts (the reference itself is single-GPU; both are additions):
   exchange the 8-byte states of every row, and each rank combines the G states
   of a row locally:  lse = M + log(sum_g s_g exp(m_g - M)).  Two exchanges:
   VocabShardExchange (the product path) has the partial kernel store the pairs
-  straight into every rank's buffer over NVLink and signal with system-scope
-  atomics, then a combine kernel waits for all ranks; vocab_sharded_logsumexp
+  straight into every rank's buffer over NVLink, then a combine kernel
+  publishes this rank's delivery (a system-scope release of the call's epoch
+  into every rank's flag word) and waits for all ranks; vocab_sharded_logsumexp
   does the same with ext.lse_partial, an NCCL all-gather and ext.lse_combine
   (the baseline, and the path for groups without peer memory).
   Every rank ends with the full (B,) result.  The association differs from a
   single-GPU pass, so results agree to rounding, not bit for bit.
+  The backward needs no exchange: with the combined lse on every rank, each
+  rank's shard gradient is g * exp(x_shard - lse), the single-GPU backward
+  kernel on its own columns (VocabShardedLogSumExp).
 
 The local compute functions are injectable so the exchange logic can be
 exercised on CPU ranks over gloo.
@@ -79,12 +83,50 @@ def vocab_sharded_logsumexp(x_shard: torch.Tensor, group=None,
     return combine_fn(gather_partials(ms, group))
 
 
+class VocabShardedLogSumExp(torch.autograd.Function):
+    """Autograd over a vocab-sharded log-sum-exp.
+
+    forward(x_shard, exchange, backward_fn): lse = exchange(x_shard) — a
+    VocabShardExchange, or any callable such as
+    `lambda x: vocab_sharded_logsumexp(x, group)` — the full (B,) result on
+    every rank.  backward: d lse / d x_shard = exp(x_shard - lse), so this
+    rank's gradient is backward_fn(g, x_shard, lse) on its own columns
+    (ext.onepass_lse_float_backward by default: fp32 shards).  g must be the
+    full gradient of the loss with respect to lse on every rank (a loss
+    computed identically on every rank from the replicated lse), not a
+    per-rank part of it.
+    """
+
+    @staticmethod
+    def forward(ctx, x_shard, exchange, backward_fn=None):
+        lse = exchange(x_shard)
+        ctx.save_for_backward(x_shard, lse)
+        ctx.backward_fn = backward_fn
+        return lse
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        x_shard, lse = ctx.saved_tensors
+        fn = ctx.backward_fn
+        if fn is None:
+            from . import ext
+            fn = ext.onepass_lse_float_backward
+        return fn(grad_output.contiguous(), x_shard, lse), None, None
+
+
+def vocab_sharded_logsumexp_grad(x_shard: torch.Tensor, exchange: Callable,
+                                 backward_fn: Optional[Callable] = None) -> torch.Tensor:
+    """Vocab-sharded log-sum-exp whose result carries a gradient to x_shard."""
+    return VocabShardedLogSumExp.apply(x_shard, exchange, backward_fn)
+
+
 class VocabShardExchange:
     """Vocab-sharded log-sum-exp with the (max, sumexp) exchange done by this
     library's own kernels over NVLink peer memory (fl_lse_vocab_exchange): the
-    partial kernel stores each row's pair into every rank's exchange buffer
-    and signals with system-scope atomics; a combine kernel waits (bounded)
-    for all ranks and finishes the rows.  No NCCL call on the data path.
+    partial kernel stores each row's pair into every rank's exchange buffer;
+    a combine kernel publishes this rank's delivery with a system-scope
+    release of the call's epoch, waits (bounded) for all ranks and finishes
+    the rows.  No NCCL call on the data path.
 
     The exchange buffer is a torch symmetric-memory allocation (peer mappings
     of every rank's buffer on every device), made once per (group, rows).

@@ -113,6 +113,66 @@ def batched_logsumexp_fp16(input: torch.Tensor) -> torch.Tensor:
 
 
 # --------------------------------------------------------------------------
+# Selective log-softmax (fused gather + LSE; no reference kernel)
+# --------------------------------------------------------------------------
+def selective_logsoftmax_rows(x: torch.Tensor, index: torch.Tensor, robust: bool = True,
+                              err_flag: torch.Tensor | None = None):
+    """(B, N) fp32/fp16 logits and (B,) int64 targets -> (logp, lse), both (B,) fp32,
+    logp[b] = x[b, index[b]] - lse[b], in one pass over each row.
+
+    An index outside [0, N) gives logp = NaN and, with `err_flag` (a zeroed int32
+    CUDA tensor of one element), sets it to 1; nothing is raised asynchronously.
+    fp16 rows use the FuseLSE16 rules (robust is ignored)."""
+    _check(x.dim() == 2, "x must be 2D (B, N)")
+    _check(x.is_cuda and x.dtype in (torch.float32, torch.float16), "x must be CUDA fp32 or fp16")
+    _check(x.is_contiguous(), "x must be contiguous")
+    _check(index.is_cuda and index.dtype == torch.int64, "index must be CUDA int64")
+    _check(index.dim() == 1 and index.size(0) == x.size(0), "index must be 1D (B) matching x")
+    _check(index.is_contiguous(), "index must be contiguous")
+    _check(index.device == x.device, "x and index must be on the same device")
+    if err_flag is not None:
+        _check(err_flag.is_cuda and err_flag.dtype == torch.int32 and err_flag.numel() >= 1,
+               "err_flag must be a CUDA int32 tensor")
+        _check(err_flag.device == x.device, "err_flag must be on x's device")
+    B, N = x.shape
+    _check(B == 0 or N > 0, "x has no columns to select from")
+    logp = torch.empty((B,), dtype=torch.float32, device=x.device)
+    lse = torch.empty((B,), dtype=torch.float32, device=x.device)
+    if B == 0:
+        return logp, lse
+    err = ptr(err_flag, ctypes.c_int) if err_flag is not None else None
+    if x.dtype == torch.float32:
+        call("fl_selective_logsoftmax_f32", ptr(x), ptr(index, ctypes.c_int64), ptr(logp), ptr(lse),
+             B, N, int(robust), err, _stream(x))
+    else:
+        call("fl_selective_logsoftmax_f16", ptr(x, ctypes.c_uint16), ptr(index, ctypes.c_int64),
+             ptr(logp), ptr(lse), B, N, err, _stream(x))
+    return logp, lse
+
+
+def selective_logsoftmax_backward(grad_output: torch.Tensor, x: torch.Tensor, lse: torch.Tensor,
+                                  index: torch.Tensor) -> torch.Tensor:
+    """grad_input[b, j] = grad_output[b] * ([j == index[b]] - exp(x[b, j] - lse[b])), fp32."""
+    _check(x.is_cuda and x.dtype == torch.float32 and x.dim() == 2 and x.is_contiguous(),
+           "x must be a contiguous 2D CUDA float32 tensor")
+    for t, name in ((grad_output, "grad_output"), (lse, "lse")):
+        _check(t.is_cuda and t.dtype == torch.float32 and t.dim() == 1 and t.is_contiguous(),
+               f"{name} must be a contiguous 1D CUDA float32 tensor")
+        _check(t.size(0) == x.size(0), f"{name} batch dimension must match x")
+        _check(t.device == x.device, f"{name} must be on x's device")
+    _check(index.is_cuda and index.dtype == torch.int64 and index.dim() == 1 and index.is_contiguous()
+           and index.size(0) == x.size(0) and index.device == x.device,
+           "index must be a contiguous 1D CUDA int64 tensor matching x")
+    B, N = x.shape
+    grad_input = torch.empty_like(x)
+    if B * N == 0:
+        return grad_input
+    call("fl_selective_logsoftmax_bwd", ptr(grad_output), ptr(x), ptr(lse),
+         ptr(index, ctypes.c_int64), ptr(grad_input), B, N, _stream(x))
+    return grad_input
+
+
+# --------------------------------------------------------------------------
 # IntLSE (lse_kernel.cu, lse_kernel_q10_6.cu)
 # --------------------------------------------------------------------------
 def _check_intlse_f32(input: torch.Tensor) -> None:

@@ -61,6 +61,38 @@ int fl_lse_f32_bwd(const float* g, const float* x, const float* lse,
                    float* gx, int64_t B, int64_t N, fl_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Selective log-softmax, fused: one pass over each row gives
+ *   lse[b]  = LSE over x[b, :]                      (as fl_lse_f32_fwd)
+ *   logp[b] = x[b, index[b]] - lse[b]
+ * Replaces the caller's two passes — torch.gather of the target logit plus
+ * one LSE call per sequence — in trl.trainer.utils.selective_log_softmax
+ * (trl 1.0.0) as used by experiment_rlhf_logsumexp/run_rlhf.py:145-157 with
+ * torch.logsumexp routed to onepass_lse_float (rlhf_timing.py:23-37).  No
+ * reference kernel.  index is int64 (B,); an index outside [0, N) gives
+ * logp[b] = NaN and, when err_flag is not NULL, sets *err_flag |= 1 (the
+ * caller zeroes it; the kernel never faults on it).  lse is required (the
+ * backward needs it).  N must be >= 1 when B > 0.
+ * fp16 input: fp32 arithmetic, empty-row value -1e30 as fl_lse_f16_fwd.
+ * ---------------------------------------------------------------------- */
+int fl_selective_logsoftmax_f32(const float* x, const int64_t* index, float* logp,
+                                float* lse, int64_t B, int64_t N, int robust,
+                                int* err_flag, fl_stream_t stream);
+int fl_selective_logsoftmax_f16(const uint16_t* x, const int64_t* index, float* logp,
+                                float* lse, int64_t B, int64_t N, int* err_flag,
+                                fl_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Selective log-softmax backward (fp32):
+ *   gx[b, j] = g[b] * ([j == index[b]] - exp(x[b, j] - lse[b]))
+ * i.e. d logp / d x scaled by the upstream gradient g (B,).  An index
+ * outside [0, N) contributes no one-hot term.  No reference counterpart
+ * (the reference differentiates only the LSE, onepass_lse_float_backward).
+ * ---------------------------------------------------------------------- */
+int fl_selective_logsoftmax_bwd(const float* g, const float* x, const float* lse,
+                                const int64_t* index, float* gx, int64_t B, int64_t N,
+                                fl_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * FuseLSE16 forward: out[b] (fp32) = LSE over x[b, :] given as IEEE fp16
  * (uint16 bit patterns), fp32 arithmetic.  Same rules as robust fp32.
  * Replaces batched_logsumexp_fp16 (fuselse/gpu/fused_fp16_kernel.cu:112-132).

@@ -152,6 +152,31 @@ def lse_bwd_f64(g: np.ndarray, x: np.ndarray, lse: np.ndarray) -> np.ndarray:
         return np.asarray(g, np.float64)[:, None] * np.exp(x - np.asarray(lse, np.float64)[:, None])
 
 
+def selective_f64(x: np.ndarray, index: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """(logp, lse) in fp64: logp[b] = x[b, index[b]] - LSE(x[b, :]) — the value of
+    trl.trainer.utils.selective_log_softmax (trl 1.0.0) as run_rlhf.py:145-157 calls
+    it; an index outside [0, N) gives NaN."""
+    x = np.asarray(x, np.float64)
+    index = np.asarray(index, np.int64)
+    lse = lse_f64(x)
+    ok = (index >= 0) & (index < x.shape[-1])
+    picked = np.take_along_axis(x, np.where(ok, index, 0)[..., None], -1)[..., 0]
+    with np.errstate(invalid="ignore"):
+        logp = np.where(ok, picked - lse, np.nan)
+    return logp, lse
+
+
+def selective_bwd_f64(g: np.ndarray, x: np.ndarray, lse: np.ndarray, index: np.ndarray) -> np.ndarray:
+    """d logp / d x scaled by g: g[b] * (onehot(index[b]) - exp(x - lse)) in fp64;
+    an index outside [0, N) adds no one-hot term."""
+    gx = -lse_bwd_f64(g, x, lse)
+    g = np.asarray(g, np.float64)
+    index = np.asarray(index, np.int64)
+    rows = np.nonzero((index >= 0) & (index < gx.shape[-1]))[0]
+    gx[rows, index[rows]] += g[rows]
+    return gx
+
+
 def sparse_f64(node_mars, element_mars, params, nids, cids, pids, block_size, floor=1e-45):
     """fp64 sparse layer: LSE_e(log(max(w, floor)) + child) for every output row
     (the formula of run_pyjuice.py:90-119, with the kernels' 1e-45 floor)."""

@@ -5,6 +5,7 @@ distributed result against the single-GPU kernels on the full input:
   * vocab shards: ext.lse_partial on the local columns + NCCL all-gather of the
     (max, sumexp) pairs + ext.lse_combine, fp16 logits of the LLM config shape
     (rows scaled down);
+  * vocab shards through the library's NVLink exchange, forward and backward;
   * batch rows: robust fp32 forward on the local rows, gathered.
 Exits non-zero on any mismatch.
 """
@@ -78,6 +79,19 @@ def main():
     err = ((got[fin] - want[fin]).abs() / want[fin].abs().clamp_min(1.0)).max().item()
     assert err <= 1e-5, f"fp32 peer exchange err {err}"
     assert not ex.error() and not ex32.error()
+    # vocab-sharded forward + backward through autograd: each rank's shard
+    # gradient equals those columns of the single-GPU backward
+    xs = x[8:, lo:hi].contiguous().requires_grad_()
+    ex_g = D.VocabShardExchange(xs.size(0), device=dev)
+    lse = D.vocab_sharded_logsumexp_grad(xs, ex_g)
+    w = torch.linspace(0.5, 2.0, lse.numel(), device=dev)  # same loss on every rank
+    (lse * w).sum().backward()
+    full = x[8:].contiguous()
+    want_g = ext.onepass_lse_float_backward(w, full, ext.onepass_lse_float_robust(full))[:, lo:hi]
+    fin_g = torch.isfinite(want_g)
+    assert torch.equal(fin_g, torch.isfinite(xs.grad)), "vocab-shard backward: special values differ"
+    gerr = (xs.grad[fin_g] - want_g[fin_g]).abs().max().item()
+    assert gerr <= 1e-6 + 1e-5 * want_g[fin_g].abs().max().item(), f"vocab-shard backward err {gerr}"
     # batch rows
     xb = W.fp32_rows(1000, 20000, seed=5, device=dev)
     r0, r1 = D.local_rows(xb.size(0))

@@ -68,6 +68,19 @@ def _worker(rank, world, port, mode, q):
             want = O.lse_f64(x.numpy())
             np.testing.assert_allclose(got.numpy(), want, rtol=1e-6)
             q.put((rank, "ok"))
+        elif mode == "vocab_grad":
+            lo, hi = D.local_columns(N)
+            xs = x[8:, lo:hi].contiguous().double().requires_grad_()
+            exchange = lambda t: D.vocab_sharded_logsumexp(t.detach().float(), partial_fn=_partial_cpu,
+                                                           combine_fn=_combine_cpu).double()
+            bwd = lambda g, xv, lse: g[:, None] * torch.exp(xv - lse[:, None])
+            lse = D.vocab_sharded_logsumexp_grad(xs, exchange, bwd)
+            w = torch.arange(1, lse.numel() + 1, dtype=torch.float64)  # same loss on every rank
+            (lse * w).sum().backward()
+            full = x[8:].double()
+            want = w[:, None] * torch.softmax(full, dim=1)[:, lo:hi]
+            np.testing.assert_allclose(xs.grad.numpy(), want.numpy(), rtol=1e-5, atol=1e-9)
+            q.put((rank, "ok"))
         elif mode == "batch":
             lo, hi = D.local_rows(B)
             lse = lambda t: torch.from_numpy(O.lse_f64(t.numpy()).astype(np.float32))
@@ -114,6 +127,11 @@ def _run(mode):
 
 def test_vocab_shard_combine_ws2():
     res = _run("vocab")
+    assert res == {0: "ok", 1: "ok"}, res
+
+
+def test_vocab_shard_backward_ws2():
+    res = _run("vocab_grad")
     assert res == {0: "ok", 1: "ok"}, res
 
 

@@ -1,8 +1,12 @@
 """CPU tests of the host layer: validation and error behaviour of the
 reference-named entry points, the torch.logsumexp delegation rules of
-make_fuselse_logsumexp, and the partitioning helpers."""
+make_fuselse_logsumexp, the partitioning helpers, and the selective
+log-softmax oracle against the caller's algorithm (torch, CPU)."""
+import numpy as np
 import pytest
 import torch
+
+from oracle import oracle as O
 
 import fuselse_b200
 from fuselse_b200 import distributed as D
@@ -85,3 +89,52 @@ def test_split_range_partitions(n, parts):
 def test_split_range_rejects_bad_index():
     with pytest.raises(ValueError):
         D.split_range(10, 2, 2)
+
+
+# ---------------------------------------------------------------- selective log-softmax
+def test_selective_oracle_matches_trl_restatement_cpu():
+    from fuselse_b200.selective import torch_selective_log_softmax
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(3, 11, 257, generator=g, dtype=torch.float64) * 4
+    idx = torch.randint(0, 257, (3, 11), generator=g)
+    want = torch_selective_log_softmax(x, idx).numpy()
+    logp, lse = O.selective_f64(x.reshape(-1, 257).numpy(), idx.reshape(-1).numpy())
+    np.testing.assert_allclose(logp.reshape(3, 11), want, rtol=1e-12, atol=1e-12)
+    np.testing.assert_allclose(lse, torch.logsumexp(x, -1).reshape(-1).numpy(), rtol=1e-12)
+
+
+def test_selective_oracle_bad_index_is_nan():
+    x = np.zeros((3, 4))
+    logp, lse = O.selective_f64(x, np.array([0, 4, -1]))
+    assert logp[0] == pytest.approx(-np.log(4)) and np.isnan(logp[1:]).all()
+
+
+def test_selective_bwd_oracle_matches_autograd_cpu():
+    from fuselse_b200.selective import torch_selective_log_softmax
+    g = torch.Generator().manual_seed(1)
+    x = (torch.randn(2, 5, 33, generator=g, dtype=torch.float64) * 3).requires_grad_()
+    idx = torch.randint(0, 33, (2, 5), generator=g)
+    up = torch.randn(2, 5, generator=g, dtype=torch.float64)
+    (torch_selective_log_softmax(x, idx) * up).sum().backward()
+    xf = x.detach().reshape(-1, 33).numpy()
+    lse = O.lse_f64(xf)
+    want = O.selective_bwd_f64(up.reshape(-1).numpy(), xf, lse, idx.reshape(-1).numpy())
+    np.testing.assert_allclose(x.grad.reshape(-1, 33).numpy(), want, rtol=1e-12, atol=1e-14)
+
+
+def test_selective_delegates_cpu_inputs_to_torch():
+    import fuselse_b200
+    from fuselse_b200.selective import torch_selective_log_softmax
+    x = torch.randn(2, 6, 50)
+    idx = torch.randint(0, 50, (2, 6))
+    torch.testing.assert_close(fuselse_b200.selective_log_softmax(x, idx),
+                               torch_selective_log_softmax(x, idx))
+
+
+def test_selective_validation_without_gpu():
+    from fuselse_b200 import ext
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ext.selective_logsoftmax_rows(torch.zeros(2, 3), torch.zeros(2, dtype=torch.int64))
+    with pytest.raises(RuntimeError, match="contiguous 2D CUDA"):
+        ext.selective_logsoftmax_backward(torch.zeros(2), torch.zeros(2, 3), torch.zeros(2),
+                                          torch.zeros(2, dtype=torch.int64))
