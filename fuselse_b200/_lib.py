@@ -24,12 +24,21 @@ _stream = c_void_p
 SIGNATURES = {
     "fl_lse_f32_fwd": [_fp, _fp, c_int64, c_int64, c_int, _stream],
     "fl_lse_f32_bwd": [_fp, _fp, _fp, _fp, c_int64, c_int64, _stream],
+    "fl_lse_f32_fwd_strided": [_fp, _fp, c_int64, c_int64, c_int64, c_int64, c_int64, c_int, _stream],
+    "fl_lse_f32_bwd_strided": [_fp, _fp, _fp, _fp, c_int64, c_int64, c_int64, c_int64, c_int64,
+                               _stream],
+    "fl_lse_f32_fwd_dim": [_fp, _fp, c_int64, c_int64, c_int64, c_int, _stream],
+    "fl_lse_f32_bwd_dim": [_fp, _fp, _fp, _fp, c_int64, c_int64, c_int64, _stream],
     "fl_lse_f16_fwd": [POINTER(c_uint16), _fp, c_int64, c_int64, _stream],
     "fl_selective_logsoftmax_f32": [_fp, POINTER(c_int64), _fp, _fp, c_int64, c_int64, c_int,
                                     POINTER(c_int), _stream],
     "fl_selective_logsoftmax_f16": [POINTER(c_uint16), POINTER(c_int64), _fp, _fp, c_int64, c_int64,
                                     POINTER(c_int), _stream],
     "fl_selective_logsoftmax_bwd": [_fp, _fp, _fp, POINTER(c_int64), _fp, c_int64, c_int64, _stream],
+    "fl_selective_logsoftmax_f32_strided": [_fp, POINTER(c_int64), _fp, _fp, c_int64, c_int64, c_int64,
+                                            c_int64, c_int64, c_int, POINTER(c_int), _stream],
+    "fl_selective_logsoftmax_bwd_strided": [_fp, _fp, _fp, POINTER(c_int64), _fp, c_int64, c_int64,
+                                            c_int64, c_int64, c_int64, _stream],
     "fl_lse_f32_partial": [_fp, _fp, c_int64, c_int64, _stream],
     "fl_lse_f16_partial": [POINTER(c_uint16), _fp, c_int64, c_int64, _stream],
     "fl_lse_combine": [_fp, _fp, c_int64, c_int64, _stream],

@@ -6,13 +6,23 @@ reference method names (`onepass_lse_float[_robust]`,
 `logsumexp(input, dim=-1, keepdim=False)`.
 
 Behaviour kept from the reference:
-  * inputs that are not CUDA fp32, not reduced over the last dim, or whose last
-    dim is < 2 are delegated to torch.logsumexp (API behaviour, not a CPU
-    kernel of this library);
+  * inputs that are not CUDA fp32, or whose reduced dim is < 2 long, are
+    delegated to torch.logsumexp (API behaviour, not a CPU kernel of this
+    library);
   * with grad enabled and input.requires_grad, an autograd Function saves the
-    flattened input and the result and calls the fused backward;
-  * otherwise 2-D contiguous inputs go straight to the forward kernel, others
-    are flattened to (-1, N) first.
+    input and the result and calls the fused backward;
+  * otherwise 2-D contiguous inputs go straight to the forward kernel.
+
+Where the reference copies (`reshape(-1, N).contiguous()`, autograd.py:19,56)
+or delegates (dim != -1, :44-49), an extension that also provides the
+in-place layouts (`fuselse_b200.ext` does) reads the tensor where it lies:
+  * last-dim reductions of non-contiguous inputs whose rows are unit-stride
+    and whose leading dims form at most two stride levels (a slice such as
+    logits[:, :-1, :]) go to the strided-row kernels;
+  * reductions over another dim of a contiguous input go to the
+    middle-dim kernels.
+Anything else is copied to a contiguous (-1, N) view as the reference does,
+or delegated to torch.logsumexp.
 """
 from __future__ import annotations
 
@@ -24,6 +34,9 @@ def make_fuselse_logsumexp(extension=None, robust: bool = True):
         from . import ext as extension
     forward_kernel = extension.onepass_lse_float_robust if robust else extension.onepass_lse_float
     backward_kernel = extension.onepass_lse_float_backward
+    in_place = all(hasattr(extension, n) for n in (
+        "row_layout", "onepass_lse_float_strided", "onepass_lse_float_backward_strided",
+        "logsumexp_dim", "logsumexp_dim_backward"))
     reference_logsumexp = torch.logsumexp
 
     class FuseLSEFunction(torch.autograd.Function):
@@ -43,22 +56,60 @@ def make_fuselse_logsumexp(extension=None, robust: bool = True):
             grad_input = backward_kernel(flat_grad, flat_input, output)
             return grad_input.reshape(ctx.input_shape)
 
+    class FuseLSEStridedFunction(torch.autograd.Function):
+        """Last-dim reduction of a strided input, read in place (no copy)."""
+
+        @staticmethod
+        def forward(ctx, input_tensor):
+            output = extension.onepass_lse_float_strided(input_tensor, robust=robust)
+            ctx.save_for_backward(input_tensor, output)
+            return output
+
+        @staticmethod
+        def backward(ctx, grad_output):
+            input_tensor, output = ctx.saved_tensors
+            return extension.onepass_lse_float_backward_strided(grad_output, input_tensor, output)
+
+    class FuseLSEDimFunction(torch.autograd.Function):
+        """Reduction over a dim other than the last of a contiguous input."""
+
+        @staticmethod
+        def forward(ctx, input_tensor, dim):
+            output = extension.logsumexp_dim(input_tensor, dim, robust=robust)
+            ctx.save_for_backward(input_tensor, output)
+            ctx.dim = dim
+            return output
+
+        @staticmethod
+        def backward(ctx, grad_output):
+            input_tensor, output = ctx.saved_tensors
+            return extension.logsumexp_dim_backward(grad_output, input_tensor, output, ctx.dim), None
+
     def logsumexp(input_tensor, dim=-1, keepdim=False):
         if isinstance(dim, (tuple, list)):
             if len(dim) != 1:
                 return reference_logsumexp(input_tensor, dim=dim, keepdim=keepdim)
             dim = dim[0]
-        normalized_dim = dim if dim >= 0 else input_tensor.dim() + dim
-        supported = (
-            input_tensor.is_cuda
-            and input_tensor.dtype == torch.float32
-            and input_tensor.dim() >= 1
-            and normalized_dim == input_tensor.dim() - 1
-            and input_tensor.shape[-1] >= 2
-        )
-        if not supported:
+        if not (input_tensor.is_cuda and input_tensor.dtype == torch.float32
+                and input_tensor.dim() >= 1):
             return reference_logsumexp(input_tensor, dim=dim, keepdim=keepdim)
-        if torch.is_grad_enabled() and input_tensor.requires_grad:
+        normalized_dim = dim if dim >= 0 else input_tensor.dim() + dim
+        last = input_tensor.dim() - 1
+        if not 0 <= normalized_dim <= last or input_tensor.shape[normalized_dim] < 2:
+            return reference_logsumexp(input_tensor, dim=dim, keepdim=keepdim)
+        grad = torch.is_grad_enabled() and input_tensor.requires_grad
+        if normalized_dim != last:
+            if not (in_place and input_tensor.is_contiguous()):
+                return reference_logsumexp(input_tensor, dim=dim, keepdim=keepdim)
+            result = (FuseLSEDimFunction.apply(input_tensor, normalized_dim) if grad
+                      else extension.logsumexp_dim(input_tensor, normalized_dim, robust=robust))
+            return result.unsqueeze(normalized_dim) if keepdim else result
+        strided = (in_place and not input_tensor.is_contiguous()
+                   and extension.row_layout(input_tensor) is not None)
+        if strided:
+            result = (FuseLSEStridedFunction.apply(input_tensor) if grad
+                      else extension.onepass_lse_float_strided(input_tensor, robust=robust))
+        elif grad:
             result = FuseLSEFunction.apply(input_tensor)
         elif input_tensor.dim() == 2 and input_tensor.is_contiguous():
             result = forward_kernel(input_tensor)

@@ -118,16 +118,28 @@ __device__ __forceinline__ float max_nan(float a, float b) {
 // ---------------------------------------------------------------------------
 // Online log-sum-exp state (m, s): m = running max (NaN-propagating),
 // s = sum exp(x - safe(m)), safe(-inf) = 0 so an all--inf prefix keeps s = 0.
+// Every exponent is taken as ex2((x - M) * log2(e)): the difference first, so
+// the max's own term is exactly 2^0, a state whose max did not change is
+// rescaled by exactly 1 (no drift over many folds and merges), and logits of
+// any magnitude keep their terms in range.  (Folding x*log2e - M*log2e into
+// one FMA would leave each term off by the rounding error of M*log2e — a
+// factor that compounds with every rescale and, for |M| beyond ~1e11,
+// overflows the sum.)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float safe_max(float m) {
     return m == -INFINITY ? 0.0f : m;
 }
 
+// exp(x - M) for a state max M already passed through safe_max.
+__device__ __forceinline__ float exp_from(float x, float Ms) {
+    return ex2((x - Ms) * kLog2e);
+}
+
 // Merge (m2, s2) into (m, s).
 __device__ __forceinline__ void ms_merge(float& m, float& s, float m2, float s2) {
     const float M = max_nan(m, m2);
-    const float Ml = safe_max(M) * kLog2e;
-    s = s * ex2(fmaf(m, kLog2e, -Ml)) + s2 * ex2(fmaf(m2, kLog2e, -Ml));
+    const float Ms = safe_max(M);
+    s = s * exp_from(m, Ms) + s2 * exp_from(m2, Ms);
     m = M;
 }
 

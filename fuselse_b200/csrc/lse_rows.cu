@@ -77,7 +77,7 @@ __device__ __forceinline__ void write_row(float* out, int64_t row, float m, floa
 template <typename T, int MODE>
 __global__ void __launch_bounds__(FwdShape<T>::kThreads) lse_segment_kernel(
     const T* __restrict__ x, float* __restrict__ out, int64_t B, int64_t N,
-    int nseg, float empty_value, SelArgs sel) {
+    int nseg, float empty_value, SelArgs sel, RowMap rm) {
     constexpr int E = Elem<T>::kPerVec;
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = static_cast<int>(blockIdx.x % nseg);
@@ -87,7 +87,7 @@ __global__ void __launch_bounds__(FwdShape<T>::kThreads) lse_segment_kernel(
     float m = -INFINITY, s = 0.0f;
     Target<T> tg;
     if (row < B) {
-        const T* rowp = x + row * N;
+        const T* rowp = x + rm(row);
         if (MODE == kOutSelect && rank == 0 && threadIdx.x == 0) tg.fetch(rowp, N, row, sel);
         const int64_t head = head_elems(rowp, N);
         const int64_t nv = (N - head) / E;
@@ -123,14 +123,15 @@ __global__ void __launch_bounds__(FwdShape<T>::kThreads) lse_segment_kernel(
 template <typename T, int MODE>
 __global__ void __launch_bounds__(kThreads) lse_warp_kernel(
     const T* __restrict__ x, float* __restrict__ out, int64_t B, int64_t N,
-    float empty_value, SelArgs sel) {
+    float empty_value, SelArgs sel, RowMap rm) {
     const int lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
     if (row >= B) return;
+    const T* rowp = x + rm(row);
     Target<T> tg;
-    if (MODE == kOutSelect && lane == 0) tg.fetch(x + row * N, N, row, sel);
+    if (MODE == kOutSelect && lane == 0) tg.fetch(rowp, N, row, sel);
     float m, s;
-    fold_row_warp(x + row * N, N, lane, m, s);
+    fold_row_warp(rowp, N, lane, m, s);
     if (lane == 0) write_row<T, MODE>(out, row, m, s, empty_value, tg, sel);
 }
 
@@ -146,32 +147,49 @@ __global__ void lse_combine_kernel(const float2* __restrict__ ms, float* __restr
     out[b] = ms_finalize(m, s, -INFINITY);
 }
 
-// gx = g[row] * exp(x - lse[row]) over chunks of one row.
+// gx = g[row] * exp(x - lse[row]) over chunks of one row; x rows placed by a
+// RowMap, gx dense (B, N).
 // SEL (selective log-softmax backward): gx = g[row] * ([j == index[row]] - exp(x - lse[row])),
 // the one-hot term added by the thread that owns column index[row].
+// A row whose x and gx starts differ in 16-byte phase (possible for strided x)
+// is done with 4-byte accesses over the same chunk split.
 constexpr int kBwdUnroll = 4;
 
 template <bool SEL>
 __global__ void __launch_bounds__(kThreads) lse_bwd_kernel(
     const float* __restrict__ g, const float* __restrict__ x,
     const float* __restrict__ lse, float* __restrict__ gx, int64_t B, int64_t N,
-    int nchunk, int64_t chunk_vec, const int64_t* __restrict__ index) {
+    int nchunk, int64_t chunk_vec, const int64_t* __restrict__ index, RowMap rm) {
     const int chunk = static_cast<int>(blockIdx.x % nchunk);
     const int64_t row = static_cast<int64_t>(blockIdx.x / nchunk);
-    const float* xr = x + row * N;
+    const float* xr = x + rm(row);
     float* gr = gx + row * N;
     const float g0 = __ldg(g + row);
     const float gs = SEL ? -g0 : g0;
-    const float ll = __ldg(lse + row) * kLog2e;
+    const float l = __ldg(lse + row);
     const int64_t head = head_elems(xr, N);
     const int64_t nv = (N - head) / 4;
     const int64_t tail0 = head + nv * 4;
     const int64_t v0 = min(nv, chunk * chunk_vec), v1 = min(nv, v0 + chunk_vec);
+    const int64_t t = SEL ? __ldg(index + row) : -1;
+    auto op = [&](float v) { return gs * exp_from(v, l); };
+    auto one = [&](int64_t j) {  // scalar column j of the row
+        float o = op(__ldg(xr + j));
+        if (SEL && j == t) o += g0;
+        gr[j] = o;
+    };
+    if (chunk == 0) {
+        if (threadIdx.x < head) one(threadIdx.x);
+        if (tail0 + threadIdx.x < N) one(tail0 + threadIdx.x);
+    }
+    if (((reinterpret_cast<uintptr_t>(xr) ^ reinterpret_cast<uintptr_t>(gr)) & 15u) != 0) {
+        for (int64_t j = head + 4 * v0 + threadIdx.x; j < head + 4 * v1; j += kThreads) one(j);
+        return;
+    }
     // target column relative to the first vector (any value when !SEL)
-    const int64_t tv = SEL ? __ldg(index + row) - head : -1;
+    const int64_t tv = t - head;
     const uint4* xv = reinterpret_cast<const uint4*>(xr + head);
     float4* gv = reinterpret_cast<float4*>(gr + head);
-    auto op = [&](float v) { return gs * ex2(fmaf(v, kLog2e, -ll)); };
     auto vec = [&](uint4 r, int64_t i) {
         float4 o = make_float4(op(__uint_as_float(r.x)), op(__uint_as_float(r.y)),
                                op(__uint_as_float(r.z)), op(__uint_as_float(r.w)));
@@ -186,11 +204,6 @@ __global__ void __launch_bounds__(kThreads) lse_bwd_kernel(
         }
         return o;
     };
-    auto one = [&](int64_t j) {  // scalar column j of the row
-        float o = op(__ldg(xr + j));
-        if (SEL && j == tv + head) o += g0;
-        gr[j] = o;
-    };
     int64_t i = v0 + threadIdx.x;
     for (; i + (kBwdUnroll - 1) * kThreads < v1; i += kBwdUnroll * kThreads) {
         uint4 r[kBwdUnroll];
@@ -200,28 +213,6 @@ __global__ void __launch_bounds__(kThreads) lse_bwd_kernel(
         for (int u = 0; u < kBwdUnroll; ++u) st_stream_f4(gv + i + u * kThreads, vec(r[u], i + u * kThreads));
     }
     for (; i < v1; i += kThreads) st_stream_f4(gv + i, vec(ld_stream_u4(xv + i), i));
-    if (chunk == 0) {
-        if (threadIdx.x < head) one(threadIdx.x);
-        if (tail0 + threadIdx.x < N) one(tail0 + threadIdx.x);
-    }
-}
-
-// Element-wise backward for x / gx buffers whose 16-byte phases differ.
-template <bool SEL>
-__global__ void lse_bwd_scalar_kernel(const float* __restrict__ g, const float* __restrict__ x,
-                                      const float* __restrict__ lse, float* __restrict__ gx,
-                                      int64_t B, int64_t N, const int64_t* __restrict__ index) {
-    const int64_t row = blockIdx.y;
-    const float g0 = __ldg(g + row);
-    const float gs = SEL ? -g0 : g0;
-    const float ll = __ldg(lse + row) * kLog2e;
-    const int64_t t = SEL ? __ldg(index + row) : -1;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < N;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        float o = gs * ex2(fmaf(__ldg(x + row * N + i), kLog2e, -ll));
-        if (SEL && i == t) o += g0;
-        gx[row * N + i] = o;
-    }
 }
 
 // ---------------------------------------------------------------------------
@@ -262,11 +253,13 @@ int choose_nseg(int64_t B, int64_t N) {
 
 template <typename T, int MODE>
 int launch_rows(const T* x, float* out, int64_t B, int64_t N, float empty_value,
-                cudaStream_t stream, const char* what, SelArgs sel = SelArgs{}) {
+                cudaStream_t stream, const char* what, SelArgs sel = SelArgs{},
+                RowMap rm = RowMap{INT64_MAX, 0, -1}) {
+    if (rm.row_stride < 0) rm = RowMap::dense(N);
     if (warp_per_row<T>(B, N)) {
         const int64_t grid = (B + kWarps - 1) / kWarps;
         FL_REQUIRE(grid <= INT32_MAX, "%s: B=%lld too large", what, (long long)B);
-        lse_warp_kernel<T, MODE><<<(unsigned)grid, kThreads, 0, stream>>>(x, out, B, N, empty_value, sel);
+        lse_warp_kernel<T, MODE><<<(unsigned)grid, kThreads, 0, stream>>>(x, out, B, N, empty_value, sel, rm);
         return check_launch(what);
     }
     const int nseg = choose_nseg<T>(B, N);
@@ -285,7 +278,7 @@ int launch_rows(const T* x, float* out, int64_t B, int64_t N, float empty_value,
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     FL_CUDA(cudaLaunchKernelEx(&cfg, lse_segment_kernel<T, MODE>, x, out, B, N, nseg,
-                               empty_value, sel));
+                               empty_value, sel, rm));
     return check_launch(what);
 }
 
@@ -365,9 +358,24 @@ extern "C" int fl_lse_combine(const float* ms, float* out, int64_t G, int64_t B,
 namespace fl {
 namespace {
 
+// Validates a strided row layout (rows of N contiguous elements, RowMap
+// placement) and returns it; rows_per_group < 0 means dense rows.
+int make_rows(int64_t B, int64_t N, int64_t rows_per_group, int64_t group_stride,
+              int64_t row_stride, RowMap* rm, const char* what) {
+    if (rows_per_group < 0) {
+        *rm = RowMap::dense(N);
+        return FL_OK;
+    }
+    FL_REQUIRE(rows_per_group >= 1 && group_stride >= 0 && row_stride >= 0,
+               "%s: bad row layout (rows_per_group %lld, strides %lld, %lld)", what,
+               (long long)rows_per_group, (long long)group_stride, (long long)row_stride);
+    *rm = RowMap{rows_per_group, group_stride, row_stride};
+    return FL_OK;
+}
+
 template <bool SEL>
 int launch_bwd(const float* g, const float* x, const float* lse, const int64_t* index, float* gx,
-               int64_t B, int64_t N, fl_stream_t stream, const char* what) {
+               int64_t B, int64_t N, RowMap rm, fl_stream_t stream, const char* what) {
     FL_REQUIRE(B >= 0 && N >= 0, "%s: negative shape", what);
     if (B == 0 || N == 0) return FL_OK;
     FL_REQUIRE(g && x && lse && gx && (!SEL || index), "%s: NULL buffer", what);
@@ -375,30 +383,20 @@ int launch_bwd(const float* g, const float* x, const float* lse, const int64_t* 
                    aligned_to(index, 8),
                "%s: misaligned buffer", what);
     if (int st = bind_device(stream, gx)) return st;
-    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    const bool same_phase = ((reinterpret_cast<uintptr_t>(x) ^ reinterpret_cast<uintptr_t>(gx)) & 15u) == 0;
-    if (!same_phase) {
-        FL_REQUIRE(B <= 65535, "%s: B=%lld too large for buffers of differing alignment", what,
-                   (long long)B);
-        const int64_t bx = std::min<int64_t>((N + 255) / 256, 1024);
-        lse_bwd_scalar_kernel<SEL><<<dim3((unsigned)bx, (unsigned)B), 256, 0, s>>>(g, x, lse, gx, B, N,
-                                                                                   index);
-        return check_launch(what);
-    }
     const int64_t nv = N / 4 + 1;
     // ~64 KB of x per CTA
     const int64_t chunk_vec = 4096;
     const int64_t nchunk = (nv + chunk_vec - 1) / chunk_vec;
     const int64_t grid = B * nchunk;
     FL_REQUIRE(grid <= INT32_MAX, "%s: B*N too large", what);
-    lse_bwd_kernel<SEL><<<(unsigned)grid, kThreads, 0, s>>>(g, x, lse, gx, B, N, (int)nchunk,
-                                                            chunk_vec, index);
+    lse_bwd_kernel<SEL><<<(unsigned)grid, kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        g, x, lse, gx, B, N, (int)nchunk, chunk_vec, index, rm);
     return check_launch(what);
 }
 
 template <typename T>
 int launch_select(const T* x, const int64_t* index, float* logp, float* lse, int64_t B, int64_t N,
-                  float empty_value, int* err_flag, fl_stream_t stream, const char* what) {
+                  RowMap rm, float empty_value, int* err_flag, fl_stream_t stream, const char* what) {
     if (int st = check_rows<T>(x, lse, B, N, what)) return st;
     FL_REQUIRE(B == 0 || (index && logp), "%s: NULL buffer", what);
     FL_REQUIRE(aligned_to(index, 8) && aligned_to(logp, 4) && aligned_to(err_flag, 4),
@@ -408,7 +406,7 @@ int launch_select(const T* x, const int64_t* index, float* logp, float* lse, int
     if (int st = bind_device(stream, lse)) return st;
     return launch_rows<T, kOutSelect>(x, lse, B, N, empty_value,
                                       reinterpret_cast<cudaStream_t>(stream), what,
-                                      SelArgs{index, logp, err_flag});
+                                      SelArgs{index, logp, err_flag}, rm);
 }
 
 }  // namespace
@@ -417,15 +415,55 @@ int launch_select(const T* x, const int64_t* index, float* logp, float* lse, int
 extern "C" int fl_lse_f32_bwd(const float* g, const float* x, const float* lse, float* gx,
                               int64_t B, int64_t N, fl_stream_t stream) {
     clear_error();
-    return launch_bwd<false>(g, x, lse, nullptr, gx, B, N, stream, "fl_lse_f32_bwd");
+    return launch_bwd<false>(g, x, lse, nullptr, gx, B, N, RowMap::dense(N), stream,
+                             "fl_lse_f32_bwd");
+}
+
+extern "C" int fl_lse_f32_fwd_strided(const float* x, float* out, int64_t B, int64_t N,
+                                      int64_t rows_per_group, int64_t group_stride,
+                                      int64_t row_stride, int robust, fl_stream_t stream) {
+    clear_error();
+    const char* what = "fl_lse_f32_fwd_strided";
+    RowMap rm;
+    if (int st = make_rows(B, N, rows_per_group, group_stride, row_stride, &rm, what)) return st;
+    if (int st = check_rows<float>(x, out, B, N, what)) return st;
+    if (B == 0) return FL_OK;
+    if (int st = bind_device(stream, out)) return st;
+    return launch_rows<float, kOutLse>(x, out, B, N, robust ? -INFINITY : -1.0e30f,
+                                       reinterpret_cast<cudaStream_t>(stream), what, SelArgs{}, rm);
+}
+
+extern "C" int fl_lse_f32_bwd_strided(const float* g, const float* x, const float* lse, float* gx,
+                                      int64_t B, int64_t N, int64_t rows_per_group,
+                                      int64_t group_stride, int64_t row_stride,
+                                      fl_stream_t stream) {
+    clear_error();
+    const char* what = "fl_lse_f32_bwd_strided";
+    RowMap rm;
+    if (int st = make_rows(B, N, rows_per_group, group_stride, row_stride, &rm, what)) return st;
+    return launch_bwd<false>(g, x, lse, nullptr, gx, B, N, rm, stream, what);
 }
 
 extern "C" int fl_selective_logsoftmax_f32(const float* x, const int64_t* index, float* logp,
                                            float* lse, int64_t B, int64_t N, int robust,
                                            int* err_flag, fl_stream_t stream) {
     clear_error();
-    return launch_select<float>(x, index, logp, lse, B, N, robust ? -INFINITY : -1.0e30f, err_flag,
-                                stream, "fl_selective_logsoftmax_f32");
+    return launch_select<float>(x, index, logp, lse, B, N, RowMap::dense(N),
+                                robust ? -INFINITY : -1.0e30f, err_flag, stream,
+                                "fl_selective_logsoftmax_f32");
+}
+
+extern "C" int fl_selective_logsoftmax_f32_strided(const float* x, const int64_t* index,
+                                                   float* logp, float* lse, int64_t B, int64_t N,
+                                                   int64_t rows_per_group, int64_t group_stride,
+                                                   int64_t row_stride, int robust, int* err_flag,
+                                                   fl_stream_t stream) {
+    clear_error();
+    const char* what = "fl_selective_logsoftmax_f32_strided";
+    RowMap rm;
+    if (int st = make_rows(B, N, rows_per_group, group_stride, row_stride, &rm, what)) return st;
+    return launch_select<float>(x, index, logp, lse, B, N, rm, robust ? -INFINITY : -1.0e30f,
+                                err_flag, stream, what);
 }
 
 extern "C" int fl_selective_logsoftmax_f16(const uint16_t* x, const int64_t* index, float* logp,
@@ -433,12 +471,26 @@ extern "C" int fl_selective_logsoftmax_f16(const uint16_t* x, const int64_t* ind
                                            fl_stream_t stream) {
     clear_error();
     return launch_select<__half>(reinterpret_cast<const __half*>(x), index, logp, lse, B, N,
-                                 -1.0e30f, err_flag, stream, "fl_selective_logsoftmax_f16");
+                                 RowMap::dense(N), -1.0e30f, err_flag, stream,
+                                 "fl_selective_logsoftmax_f16");
 }
 
 extern "C" int fl_selective_logsoftmax_bwd(const float* g, const float* x, const float* lse,
                                            const int64_t* index, float* gx, int64_t B, int64_t N,
                                            fl_stream_t stream) {
     clear_error();
-    return launch_bwd<true>(g, x, lse, index, gx, B, N, stream, "fl_selective_logsoftmax_bwd");
+    return launch_bwd<true>(g, x, lse, index, gx, B, N, RowMap::dense(N), stream,
+                            "fl_selective_logsoftmax_bwd");
+}
+
+extern "C" int fl_selective_logsoftmax_bwd_strided(const float* g, const float* x,
+                                                   const float* lse, const int64_t* index,
+                                                   float* gx, int64_t B, int64_t N,
+                                                   int64_t rows_per_group, int64_t group_stride,
+                                                   int64_t row_stride, fl_stream_t stream) {
+    clear_error();
+    const char* what = "fl_selective_logsoftmax_bwd_strided";
+    RowMap rm;
+    if (int st = make_rows(B, N, rows_per_group, group_stride, row_stride, &rm, what)) return st;
+    return launch_bwd<true>(g, x, lse, index, gx, B, N, rm, stream, what);
 }

@@ -58,6 +58,21 @@ struct FwdShape<__half> {
     static constexpr bool kWarpPipe = FL_F16_WARP_PIPE;
 };
 
+// Where row r of a (B, N) operand starts, in elements.  Rows are contiguous
+// runs of N elements; the rows themselves may be strided in two levels, as
+// the leading dims of a sliced tensor such as logits[:, :-1, :]:
+//   r * row_stride                                    for r < rows_per_group
+//   (r / rows_per_group) * group_stride + (r % rows_per_group) * row_stride
+// A dense operand has rows_per_group >= B and row_stride = N.
+struct RowMap {
+    int64_t rows_per_group, group_stride, row_stride;
+    __host__ __device__ static RowMap dense(int64_t N) { return RowMap{INT64_MAX, 0, N}; }
+    __device__ __forceinline__ int64_t operator()(int64_t r) const {
+        if (r < rows_per_group) return r * row_stride;
+        return (r / rows_per_group) * group_stride + (r % rows_per_group) * row_stride;
+    }
+};
+
 // Element traits: how many elements one 16-byte vector carries and how to
 // widen them to fp32.
 template <typename T>
@@ -105,11 +120,11 @@ __device__ __forceinline__ void ms_fold(float& m, float& s, const float* v) {
 #pragma unroll
         for (int i = 0; i + w < K; i += 2 * w) t[i] = max_nan(t[i], t[i + w]);
     const float M = max_nan(m, t[0]);
-    const float Ml = safe_max(M) * kLog2e;
-    float a0 = s * ex2(fmaf(m, kLog2e, -Ml));
+    const float Ms = safe_max(M);
+    float a0 = s * exp_from(m, Ms);
     float a1 = 0.0f;
     auto e = [&](int i) {
-        const float t = fmaf(v[i], kLog2e, -Ml);
+        const float t = (v[i] - Ms) * kLog2e;
         constexpr int P = POLY > 0 ? POLY : 1;
         return (POLY > 0 && i % P == P - 1) ? ex2_poly(t) : ex2(t);
     };

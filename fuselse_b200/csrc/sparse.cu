@@ -102,11 +102,11 @@ struct Acc<false, VEC, ET> {
 #pragma unroll
             for (int g = 1; g < kGroup; ++g) mx = max_nan(mx, lg[g][c]);
             const float M = max_nan(m[c], mx);
-            const float Ml = safe_max(M) * kLog2e;
-            float a = s[c] * ex2(fmaf(m[c], kLog2e, -Ml));
+            const float Ms = safe_max(M);
+            float a = s[c] * exp_from(m[c], Ms);
 #pragma unroll
             for (int g = 0; g < kGroup; ++g)
-                if (g < nvalid) a += ex2(fmaf(lg[g][c], kLog2e, -Ml));
+                if (g < nvalid) a += exp_from(lg[g][c], Ms);
             s[c] = a;
             m[c] = M;
         }

@@ -6,9 +6,9 @@
 //     into (m, s) = (max, sum exp(x - m)) and stores the pair straight into
 //     every rank's exchange buffer (P2P stores through the peer mappings of a
 //     symmetric allocation).  It has no epilogue: no fence, no counter.
-//   kernel 2 (vocab_combine_kernel, one thread per row): every CTA first
-//     publishes — threads 0..G-1 store the call's epoch into this rank's flag
-//     word of every rank's buffer (release, system scope).  Kernel 1 finished
+//   kernel 2 (vocab_combine_kernel, one thread per row): with G > 1 every CTA
+//     first publishes — threads 0..G-1 store the call's epoch into this rank's
+//     flag word of every rank's buffer (release, system scope).  Kernel 1 finished
 //     before kernel 2 started (stream order), so the release covers every pair
 //     this rank delivered; the store is idempotent (every CTA stores the same
 //     epoch), so no CTA depends on another having been scheduled.  Then every
@@ -16,7 +16,8 @@
 //     scope; bounded by an iteration cap and a 2 s clock limit, after which it
 //     writes NaN rows and sets a sticky error word), merges the G pairs of
 //     each row and finishes lse = M + log(sum_g s_g exp(m_g - M)); the last
-//     CTA to finish advances the call epoch.
+//     CTA to finish advances the call epoch.  With G == 1 there is nothing to
+//     publish or wait for: stream order already covers the rank's own pairs.
 // The epoch lives in the buffer, so captured CUDA graphs replay correctly;
 // pairs alternate between two slots by epoch parity.  A rank's flag reaches
 // epoch k only once that rank has finished call k-1 entirely, so a rank that
@@ -98,12 +99,14 @@ __global__ void __launch_bounds__(kCombineThreads) vocab_combine_kernel(
     uint32_t* header = reinterpret_cast<uint32_t*>(local);
     const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(header + 2);
     if (threadIdx.x == 0) timed_out = 0;
-    for (int q = threadIdx.x; q < G; q += kCombineThreads) {
-        __threadfence_system();
+    // G == 1: the only pairs are this rank's own, ordered by the stream.
+    // Otherwise the release store (a system-scope release: cumulative over the
+    // scatter kernel's stores, which precede this kernel in stream order)
+    // publishes this rank's delivery.
+    for (int q = threadIdx.x; G > 1 && q < G; q += kCombineThreads)
         st_release_sys(reinterpret_cast<uint32_t*>(peers[q] + kHeaderBytes) + rank, epoch);
-    }
     __syncthreads();
-    for (int q = threadIdx.x; q < G; q += kCombineThreads) {
+    for (int q = threadIdx.x; G > 1 && q < G; q += kCombineThreads) {
         const uint32_t* flag = reinterpret_cast<const uint32_t*>(local + kHeaderBytes) + q;
         const uint64_t t0 = global_ns();
         for (uint32_t it = 0;; ++it) {

@@ -173,6 +173,157 @@ def selective_logsoftmax_backward(grad_output: torch.Tensor, x: torch.Tensor, ls
 
 
 # --------------------------------------------------------------------------
+# In-place layouts: strided rows and dim != -1 (no contiguous copy)
+# --------------------------------------------------------------------------
+def row_layout(x: torch.Tensor):
+    """(B, N, rows_per_group, group_stride, row_stride) when the rows of x
+    (its last dim, unit stride) can be addressed where they lie: the leading
+    dims, after merging the ones that nest densely, form at most two levels.
+    None otherwise (the caller copies)."""
+    if x.dim() == 0:
+        return None
+    N = x.size(-1)
+    if N > 1 and x.stride(-1) != 1:
+        return None
+    B = 1
+    levels: list[list[int]] = []  # [size, stride], outer to inner
+    for size, stride in zip(x.shape[:-1], x.stride()[:-1]):
+        B *= size
+        if size == 1:
+            continue
+        if levels and levels[-1][1] == stride * size:
+            levels[-1] = [levels[-1][0] * size, stride]
+        else:
+            levels.append([size, stride])
+    if not levels:
+        return (B, N, -1, 0, N)
+    if len(levels) == 1:
+        return (B, N, levels[0][0], 0, levels[0][1])
+    if len(levels) == 2:
+        return (B, N, levels[1][0], levels[0][1], levels[1][1])
+    return None
+
+
+def _strided_rows(x: torch.Tensor):
+    _check(x.is_cuda and x.dtype == torch.float32, "x must be CUDA float32")
+    lay = row_layout(x)
+    _check(lay is not None, "x rows cannot be addressed in place (more than two leading stride levels)")
+    return lay
+
+
+def onepass_lse_float_strided(x: torch.Tensor, robust: bool = True) -> torch.Tensor:
+    """Log-sum-exp over the last dim of a strided fp32 tensor (..., N) read in
+    place, e.g. logits[:, :-1, :]; result shape x.shape[:-1]."""
+    B, N, rpg, gs, rs = _strided_rows(x)
+    out = torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device)
+    if B == 0:
+        return out
+    call("fl_lse_f32_fwd_strided", ptr(x), ptr(out), B, N, rpg, gs, rs, int(robust), _stream(x))
+    return out
+
+
+def onepass_lse_float_backward_strided(grad_output: torch.Tensor, x: torch.Tensor,
+                                       lse: torch.Tensor) -> torch.Tensor:
+    """Dense grad_input of x's shape = grad_output[..., None] * exp(x - lse[..., None]), x read in place."""
+    B, N, rpg, gs, rs = _strided_rows(x)
+    g = grad_output.reshape(-1).contiguous()
+    lse = lse.reshape(-1).contiguous()
+    _check(g.numel() == B and lse.numel() == B, "grad_output / lse must have x.shape[:-1]")
+    _check(g.dtype == torch.float32 and lse.dtype == torch.float32 and g.device == x.device
+           and lse.device == x.device, "grad_output and lse must be CUDA float32 on x's device")
+    grad_input = torch.empty(x.shape, dtype=torch.float32, device=x.device)
+    if B * N == 0:
+        return grad_input
+    call("fl_lse_f32_bwd_strided", ptr(g), ptr(x), ptr(lse), ptr(grad_input), B, N, rpg, gs, rs,
+         _stream(x))
+    return grad_input
+
+
+def _dim_view(x: torch.Tensor, dim: int):
+    _check(x.is_cuda and x.dtype == torch.float32, "x must be CUDA float32")
+    _check(x.is_contiguous(), "x must be contiguous")
+    d = dim if dim >= 0 else dim + x.dim()
+    _check(0 <= d < x.dim(), f"dim {dim} out of range for {x.dim()}-D input")
+    outer = 1
+    for s in x.shape[:d]:
+        outer *= s
+    inner = 1
+    for s in x.shape[d + 1:]:
+        inner *= s
+    return d, outer, x.size(d), inner
+
+
+def logsumexp_dim(x: torch.Tensor, dim: int, robust: bool = True) -> torch.Tensor:
+    """Log-sum-exp of a contiguous fp32 tensor over any dim, read in place."""
+    d, outer, N, inner = _dim_view(x, dim)
+    out = torch.empty(x.shape[:d] + x.shape[d + 1:], dtype=torch.float32, device=x.device)
+    if outer * inner == 0:
+        return out
+    call("fl_lse_f32_fwd_dim", ptr(x), ptr(out), outer, N, inner, int(robust), _stream(x))
+    return out
+
+
+def logsumexp_dim_backward(grad_output: torch.Tensor, x: torch.Tensor, lse: torch.Tensor,
+                           dim: int) -> torch.Tensor:
+    """grad_input = grad_output * exp(x - lse), broadcast over `dim`."""
+    d, outer, N, inner = _dim_view(x, dim)
+    g = grad_output.contiguous()
+    lse = lse.contiguous()
+    _check(g.numel() == outer * inner and lse.numel() == outer * inner,
+           "grad_output / lse must have x's shape without dim")
+    _check(g.dtype == torch.float32 and lse.dtype == torch.float32 and g.device == x.device
+           and lse.device == x.device, "grad_output and lse must be CUDA float32 on x's device")
+    grad_input = torch.empty_like(x)
+    if x.numel() == 0:
+        return grad_input
+    call("fl_lse_f32_bwd_dim", ptr(g), ptr(x), ptr(lse), ptr(grad_input), outer, N, inner,
+         _stream(x))
+    return grad_input
+
+
+def selective_logsoftmax_strided(x: torch.Tensor, index: torch.Tensor, robust: bool = True,
+                                 err_flag: torch.Tensor | None = None):
+    """selective_logsoftmax_rows for fp32 logits (..., N) whose rows are read in
+    place (e.g. logits[:, :-1, :]); index has x.shape[:-1]; returns (logp, lse)
+    flattened to (B,)."""
+    B, N, rpg, gs, rs = _strided_rows(x)
+    t = index.reshape(-1).to(torch.int64).contiguous()
+    _check(t.is_cuda and t.numel() == B and t.device == x.device, "index must have x.shape[:-1] on x's device")
+    _check(B == 0 or N > 0, "x has no columns to select from")
+    if err_flag is not None:
+        _check(err_flag.is_cuda and err_flag.dtype == torch.int32 and err_flag.device == x.device,
+               "err_flag must be a CUDA int32 tensor on x's device")
+    logp = torch.empty((B,), dtype=torch.float32, device=x.device)
+    lse = torch.empty((B,), dtype=torch.float32, device=x.device)
+    if B == 0:
+        return logp, lse
+    err = ptr(err_flag, ctypes.c_int) if err_flag is not None else None
+    call("fl_selective_logsoftmax_f32_strided", ptr(x), ptr(t, ctypes.c_int64), ptr(logp), ptr(lse),
+         B, N, rpg, gs, rs, int(robust), err, _stream(x))
+    return logp, lse
+
+
+def selective_logsoftmax_backward_strided(grad_output: torch.Tensor, x: torch.Tensor,
+                                          lse: torch.Tensor, index: torch.Tensor) -> torch.Tensor:
+    """Dense grad_input of x's shape for the strided selective log-softmax."""
+    B, N, rpg, gs, rs = _strided_rows(x)
+    g = grad_output.reshape(-1).contiguous()
+    lse = lse.reshape(-1).contiguous()
+    t = index.reshape(-1).to(torch.int64).contiguous()
+    _check(g.numel() == B and lse.numel() == B and t.numel() == B,
+           "grad_output, lse and index must have x.shape[:-1]")
+    _check(g.dtype == torch.float32 and lse.dtype == torch.float32 and g.device == x.device
+           and lse.device == x.device and t.device == x.device,
+           "grad_output and lse must be CUDA float32 on x's device")
+    grad_input = torch.empty(x.shape, dtype=torch.float32, device=x.device)
+    if B * N == 0:
+        return grad_input
+    call("fl_selective_logsoftmax_bwd_strided", ptr(g), ptr(x), ptr(lse), ptr(t, ctypes.c_int64),
+         ptr(grad_input), B, N, rpg, gs, rs, _stream(x))
+    return grad_input
+
+
+# --------------------------------------------------------------------------
 # IntLSE (lse_kernel.cu, lse_kernel_q10_6.cu)
 # --------------------------------------------------------------------------
 def _check_intlse_f32(input: torch.Tensor) -> None:

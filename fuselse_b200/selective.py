@@ -54,6 +54,22 @@ class SelectiveLogSoftmax(torch.autograd.Function):
         return grad, None, None, None
 
 
+class SelectiveLogSoftmaxStrided(torch.autograd.Function):
+    """fp32 logits (..., V) whose rows are read in place (e.g. logits[:, :-1, :])."""
+
+    @staticmethod
+    def forward(ctx, logits, targets, robust, err_flag):
+        logp, lse = ext.selective_logsoftmax_strided(logits, targets, robust=robust, err_flag=err_flag)
+        ctx.save_for_backward(logits, lse, targets)
+        return logp
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        logits, lse, targets = ctx.saved_tensors
+        grad = ext.selective_logsoftmax_backward_strided(grad_output, logits, lse, targets)
+        return grad, None, None, None
+
+
 def selective_log_softmax(logits: torch.Tensor, index: torch.Tensor, robust: bool = True,
                           check_index: bool = False) -> torch.Tensor:
     """Log-probabilities of `index` under softmax(logits, -1), shape index.shape.
@@ -69,10 +85,21 @@ def selective_log_softmax(logits: torch.Tensor, index: torch.Tensor, robust: boo
     if not supported:
         return torch_selective_log_softmax(logits, index)
     V = logits.shape[-1]
-    rows = logits.reshape(-1, V).contiguous()
     targets = index.reshape(-1).to(torch.int64).contiguous()
     err = torch.zeros(1, dtype=torch.int32, device=logits.device) if check_index else None
-    if logits.dtype == torch.float32 and torch.is_grad_enabled() and logits.requires_grad:
+    grad = torch.is_grad_enabled() and logits.requires_grad
+    if (logits.dtype == torch.float32 and not logits.is_contiguous()
+            and ext.row_layout(logits) is not None):
+        # strided rows (a slice such as logits[:, :-1, :]): read in place, no copy
+        if grad:
+            logp = SelectiveLogSoftmaxStrided.apply(logits, targets, robust, err)
+        else:
+            logp, _ = ext.selective_logsoftmax_strided(logits, targets, robust=robust, err_flag=err)
+        if check_index and int(err.item()):
+            raise RuntimeError(f"selective_log_softmax: index out of range for {V} classes")
+        return logp.reshape(index.shape)
+    rows = logits.reshape(-1, V).contiguous()
+    if logits.dtype == torch.float32 and grad:
         logp = SelectiveLogSoftmax.apply(rows, targets, robust, err)
     else:
         logp, _ = ext.selective_logsoftmax_rows(rows, targets, robust=robust, err_flag=err)

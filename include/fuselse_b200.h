@@ -61,6 +61,39 @@ int fl_lse_f32_bwd(const float* g, const float* x, const float* lse,
                    float* gx, int64_t B, int64_t N, fl_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Strided rows (no contiguous copy).  Row r of x (N contiguous elements)
+ * starts at element
+ *     r * row_stride                                   if r < rows_per_group
+ *     (r / rows_per_group) * group_stride + (r % rows_per_group) * row_stride
+ * — the leading two dims of a sliced tensor such as logits[:, :-1, :]
+ * (rows_per_group = T - 1, group_stride = T*V, row_stride = V).
+ * rows_per_group < 0 means dense rows (row_stride N).  out, lse, g and gx
+ * stay dense (B,) / (B, N).  The reference reduces a contiguous copy made by
+ * its autograd wrapper (fuselse/gpu/autograd.py:19,56); no reference
+ * counterpart.
+ * ---------------------------------------------------------------------- */
+int fl_lse_f32_fwd_strided(const float* x, float* out, int64_t B, int64_t N,
+                           int64_t rows_per_group, int64_t group_stride,
+                           int64_t row_stride, int robust, fl_stream_t stream);
+int fl_lse_f32_bwd_strided(const float* g, const float* x, const float* lse,
+                           float* gx, int64_t B, int64_t N, int64_t rows_per_group,
+                           int64_t group_stride, int64_t row_stride,
+                           fl_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Reduction over a dim that is not the last: x dense, viewed as
+ * (outer, N, inner), out[o, i] = LSE_n x[o, n, i] and
+ * gx[o, n, i] = g[o, i] * exp(x[o, n, i] - lse[o, i]); out, g, lse are
+ * (outer, inner).  inner == 1 is the row case.  The reference delegates
+ * dim != -1 to torch.logsumexp (fuselse/gpu/autograd.py:44-49); no
+ * reference counterpart.
+ * ---------------------------------------------------------------------- */
+int fl_lse_f32_fwd_dim(const float* x, float* out, int64_t outer, int64_t N,
+                       int64_t inner, int robust, fl_stream_t stream);
+int fl_lse_f32_bwd_dim(const float* g, const float* x, const float* lse, float* gx,
+                       int64_t outer, int64_t N, int64_t inner, fl_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Selective log-softmax, fused: one pass over each row gives
  *   lse[b]  = LSE over x[b, :]                      (as fl_lse_f32_fwd)
  *   logp[b] = x[b, index[b]] - lse[b]
@@ -80,6 +113,12 @@ int fl_selective_logsoftmax_f32(const float* x, const int64_t* index, float* log
 int fl_selective_logsoftmax_f16(const uint16_t* x, const int64_t* index, float* logp,
                                 float* lse, int64_t B, int64_t N, int* err_flag,
                                 fl_stream_t stream);
+/* Strided rows as fl_lse_f32_fwd_strided; index, logp, lse dense (B,). */
+int fl_selective_logsoftmax_f32_strided(const float* x, const int64_t* index, float* logp,
+                                        float* lse, int64_t B, int64_t N,
+                                        int64_t rows_per_group, int64_t group_stride,
+                                        int64_t row_stride, int robust, int* err_flag,
+                                        fl_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Selective log-softmax backward (fp32):
@@ -91,6 +130,11 @@ int fl_selective_logsoftmax_f16(const uint16_t* x, const int64_t* index, float* 
 int fl_selective_logsoftmax_bwd(const float* g, const float* x, const float* lse,
                                 const int64_t* index, float* gx, int64_t B, int64_t N,
                                 fl_stream_t stream);
+/* Strided x rows as fl_lse_f32_fwd_strided; gx dense (B, N). */
+int fl_selective_logsoftmax_bwd_strided(const float* g, const float* x, const float* lse,
+                                        const int64_t* index, float* gx, int64_t B, int64_t N,
+                                        int64_t rows_per_group, int64_t group_stride,
+                                        int64_t row_stride, fl_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * FuseLSE16 forward: out[b] (fp32) = LSE over x[b, :] given as IEEE fp16

@@ -215,3 +215,42 @@ def test_vocab_exchange_rejects_bad_shapes(ext):
         ex(torch.zeros(5, 10, device="cuda"))
     with pytest.raises(RuntimeError):
         ex(torch.zeros(4, 10, device="cuda", dtype=torch.float64))
+
+
+@pytest.mark.parametrize("scale", [1e6, 1e12, 1e25, 1e37])
+def test_fwd_bwd_large_magnitudes(ext, scale):
+    """Logits far beyond any realistic range: the sum keeps the max's own term
+    at exactly 1, so the result is the max plus log of a count of ties (the
+    reference's pair max + log(1 + exp(min - max)) gives the same), never
+    +-inf from an overflowing rescale."""
+    B, N = 37, 5003
+    x = _randn(B, N, seed=int(np.log10(scale)), scale=scale)
+    x[3, 17] = x[3].max() + 0  # a duplicated max in one row
+    x[3, 4000] = x[3, 17]
+    lse = ext.onepass_lse_float_robust(x)
+    want = O.lse_f64(x.cpu().numpy())
+    _close(lse.cpu().numpy(), want, RTOL32, f"scale {scale:g}")
+    assert np.isfinite(lse.cpu().numpy()).all()
+    g = torch.ones(B, device="cuda")
+    gx = ext.onepass_lse_float_backward(g, x, lse).cpu().numpy().astype(np.float64)
+    want_gx = O.lse_bwd_f64(g.cpu().numpy(), x.cpu().numpy(), lse.cpu().numpy())
+    np.testing.assert_allclose(gx, want_gx, rtol=1e-5, atol=1e-6)
+    ref = None
+    try:
+        ref = ref_ext_or_skip("ref_fused_fp32")
+    except pytest.skip.Exception:
+        pass
+    if ref is not None and scale <= 1e25:
+        _close(lse.cpu().numpy(), ref.onepass_lse_float_robust(x).cpu().numpy(), RTOL32, "vs reference")
+
+
+def test_state_does_not_drift_over_many_merges(ext):
+    """Many folds of rows whose max stays put (the first element is the max):
+    the result matches fp64 to a few ulp of the row's lse, not to a bound that
+    grows with the number of folds."""
+    B, N = 8, 1 << 20
+    x = _randn(B, N, seed=5, scale=0.01)
+    x[:, 0] = 40.0
+    lse = ext.onepass_lse_float_robust(x).cpu().numpy().astype(np.float64)
+    want = O.lse_f64(x.cpu().numpy())
+    assert np.abs(lse - want).max() <= 8 * np.spacing(np.float32(40.0 + np.log(N)))

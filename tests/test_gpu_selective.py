@@ -7,7 +7,9 @@ run with torch on the GPU, for values and for gradients through autograd.
 
 Tolerance: the log-probability inherits the LSE's error, so |logp - want| is
 held to 1e-5 x max(|lse|, 1) (fp32 and fp16 input, both computed in fp32);
-gradients (softmax values <= 1 times g) to 1e-6 absolute + 1e-5 relative.
+gradients given the same lse to 1e-6 absolute + 1e-5 relative; gradients
+compared with torch's (computed from torch's lse) to a relative 1e-5 x
+max(|lse|, 1), the forward's bound, since d(softmax)/softmax = -d(lse).
 """
 import numpy as np
 import pytest
@@ -170,7 +172,7 @@ def test_autograd_vs_trl_restatement(shape):
     assert y1.shape == y2.shape == idx.shape and y1.dtype == torch.float32
     lse = torch.logsumexp(x0, -1).abs().clamp_min(1.0)
     assert ((y1 - y2).abs() / lse).max().item() <= RTOL
-    torch.testing.assert_close(x1.grad, x2.grad, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(x1.grad, x2.grad, rtol=RTOL * lse.max().item(), atol=1e-6)
 
 
 def test_f16_result_dtype_and_value():

@@ -138,3 +138,16 @@ def test_selective_validation_without_gpu():
     with pytest.raises(RuntimeError, match="contiguous 2D CUDA"):
         ext.selective_logsoftmax_backward(torch.zeros(2), torch.zeros(2, 3), torch.zeros(2),
                                           torch.zeros(2, dtype=torch.int64))
+
+
+# ---------------------------------------------------------------- in-place row layouts
+def test_row_layout_cases():
+    x = torch.zeros(3, 18, 1001)
+    assert ext.row_layout(x) == (54, 1001, 54, 0, 1001)                 # dense: one level
+    assert ext.row_layout(x[:, :-1, :]) == (51, 1001, 17, 18 * 1001, 1001)
+    assert ext.row_layout(x[::2]) == (36, 1001, 18, 2 * 18 * 1001, 1001)  # every other group
+    assert ext.row_layout(x[:, ::2, :]) == (27, 1001, 27, 0, 2002)       # nests: one level
+    assert ext.row_layout(x[:, :, 5:]) == (54, 996, 54, 0, 1001)
+    assert ext.row_layout(torch.zeros(4, 5, 6, 7)[:, ::2, ::2, :]) is None  # three levels
+    assert ext.row_layout(x.transpose(1, 2)) is None                      # last dim not unit-stride
+    assert ext.row_layout(torch.zeros(1, 1, 9)) == (1, 9, -1, 0, 9)
