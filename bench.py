@@ -1,7 +1,7 @@
 """Benchmark of the row log-sum-exp hot path on B200 (driver contract).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload fwdbwd_f32|fwd_f32|sls_f32|f16_vocab|intlse_q16|intlse_q10_6|sparse_f32|sparse_q16]
+                    [--workload fwdbwd_f32|fwd_f32|sls_f32|f16_vocab|intlse_q16|intlse_q10_6|sparse_f32|sparse_q16|sparse_fwdbwd_f32]
 
 One JSON line on rank 0.  Default workload (the headline, BASELINE metric):
 FuseLSE fp32 forward + backward over (B, N) = (512, 128256), x ~ N(0, 1),
@@ -323,6 +323,52 @@ class Sparse(Workload):
         return self.S
 
 
+class SparseFwdBwd(Workload):
+    """Sparse PC sum layer forward + backward (fp32) on the default layer:
+    the forward kernel, then fl_sparse_f32_bwd (parameter gradients
+    node-major, element gradients child-major over the parent index built
+    once, outside the timed region) with a fixed upstream gradient."""
+    name = "sparse_fwdbwd_f32"
+    dtype = "f32"
+
+    def __init__(self, dev, seed):
+        from fuselse_b200 import ext, workloads as W
+        self.ext = ext
+        self.args = W.sparse_layer(seed=seed, device=dev)
+        node, em, params, nids, cids, pids, bs = self.args
+        P, batch = em.shape
+        S, E = cids.shape
+        self.parents = ext.sparse_parent_index(nids, cids, pids, bs, P)
+        g = torch.Generator(device=dev).manual_seed(seed + 3)
+        self.G = torch.randn(node.shape, generator=g, device=dev)
+        self.gem = torch.zeros_like(em)
+        self.gw = torch.zeros_like(params)
+        self.fwd_bytes = P * batch * 4 + S * batch * 4 + S * E * (8 + 8 + 4) + S * 8
+        # em read, em grads read + written, node rows and their grads read,
+        # param grads read + written, the edges' cids/pids, nids, and the
+        # parent-unit index (child_ptr, unit node and parameter rows)
+        self.bwd_bytes = (3 * P * batch * 4 + 2 * S * batch * 4 + S * E * (8 + 8 + 4 + 4 + 16)
+                          + S * 8 + (P + 1) * 8)
+        self.config = {"workload": f"sparse PC sum layer fp32 forward + backward: P={P}, S={S}, "
+                                   f"E={E}, batch={batch}", "l2": "inputs larger than L2, steps back to back"}
+        self.launches_per_step = 3
+
+    def _fwd(self):
+        self.ext.sparse_forward_float(*self.args)
+
+    def _bwd(self):
+        node, em, params, nids, cids, pids, bs = self.args
+        self.ext.sparse_backward_float(node, self.G, em, params, nids, cids, pids, bs,
+                                       element_grads=self.gem, param_grads=self.gw,
+                                       parents=self.parents)
+
+    def kernels(self):
+        return [("sparse_f32", self._fwd, self.fwd_bytes), ("sparse_bwd", self._bwd, self.bwd_bytes)]
+
+    def rows(self):
+        return self.args[4].size(0)
+
+
 def make_workload(name, dev, seed, world, rank):
     if name == "fwdbwd_f32":
         return FwdBwdF32(dev, seed)
@@ -346,6 +392,8 @@ def make_workload(name, dev, seed, world, rank):
         return Sparse(dev, seed, q16=False)
     if name == "sparse_q16":
         return Sparse(dev, seed, q16=True)
+    if name == "sparse_fwdbwd_f32":
+        return SparseFwdBwd(dev, seed)
     raise SystemExit(f"unknown workload {name}")
 
 

@@ -1,0 +1,340 @@
+// Backward of the sparse probabilistic-circuit sum layer (fp32).  The
+// reference has a forward only (experiment_pyjuice/sparse_float_kernel.cu);
+// this is the gradient of that forward.  With
+//   nm[n, b] = LSE_e( lw[k, e, p] + em[c_e, b] ),  n = nids[k] + p,
+//   lw = log(max(params[pids[k, e] + p], 1e-45)),  c_e = cids[k, e],
+// and an upstream gradient G[n, b] = d loss / d nm[n, b]:
+//   d loss / d em[c, b]  = sum over edges (k, e, p) with c_e = c of
+//                          G[n, b] * exp(lw + em[c, b] - nm[n, b])
+//   d loss / d params[q] = sum over edges with pids[k, e] + p = q, and over b, of
+//                          G[n, b] * exp(em[c_e, b] - nm[n, b])     (0 where the
+//                          weight is at or below the 1e-45 clamp)
+// (pyjuice's element flows and parameter flows are these with G = node
+// flows; its parameter flow is the parameter gradient times the weight).
+// A node whose nm is -inf passes no gradient.  Both results are added to
+// the caller's buffers.
+//
+// Two kernels, each reading the layer where it lies:
+//   * parameters, node-major (the forward's gather pattern): one warp per
+//     output row n; lane e holds edge e's child and parameter index (one
+//     coalesced load per 32 edges, broadcast by shuffles, so no chain of
+//     dependent index loads per edge); per column chunk G and nm of the row
+//     sit in registers while children's rows are gathered 4 at a time
+//     (16-byte loads); lane e keeps edge e's batch sum and adds it once
+//     (parameters may be tied, hence the atomic);
+//   * elements, child-major: the parents of each child come from a
+//     child -> parent-unit index built once per layer structure by the caller
+//     (CSR over units (edge, p < block_size) with each unit's node row and
+//     parameter index stored directly, so a warp resolves 32 parents with one
+//     coalesced load and one load of their weights); a warp covers a group of
+//     TPW column tiles of one child, groups ordered group-major so the group's
+//     slice of the parents' G and nm rows stays in L2 (evict-last) while the
+//     element rows stream (evict-first); 8 / TPW parents' rows in flight; the
+//     sum is formed in registers and added once: no float atomics and a fixed
+//     order, so the result is deterministic.
+#include "common.cuh"
+
+#include <algorithm>
+
+namespace fl {
+namespace {
+
+constexpr int kWarpsPerCta = 8;
+constexpr int kEdgesInFlight = 4;  // children's rows gathered per step (parameter kernel)
+
+// Column tiles (of 32 * VEC columns) per warp in the element kernel; 8 / TPW
+// parents are in flight per step.
+#ifndef FL_SPBWD_TILES_PER_WARP
+#define FL_SPBWD_TILES_PER_WARP 4
+#endif
+
+__device__ __forceinline__ float log_weight(float w) { return __logf(fmaxf(w, 1e-45f)); }
+
+struct SparseBwdArgs {
+    const float* node_mars;
+    const float* node_grads;
+    const float* em;
+    const float* params;
+    const int64_t* nids;
+    const int64_t* cids;
+    const int64_t* pids;
+    const int64_t* child_ptr;   // (num_elements + 1,): units of child c at [ptr[c], ptr[c+1])
+    const int64_t* unit_node;   // node row of each parent unit, grouped by child
+    const int64_t* unit_param;  // parameter index of each parent unit
+    int64_t num_units;
+    float* em_grads;
+    float* param_grads;
+    int64_t num_nodes, num_elements, num_params, num_nblocks, batch;
+    int E, block_size;
+    int* err;
+};
+
+// L2 policy for rows that are gathered repeatedly within a column range.
+__device__ __forceinline__ uint64_t evict_last_policy() {
+    uint64_t p;
+    asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// VEC columns of a row at column b (columns past the batch read as fill).
+template <int VEC>
+__device__ __forceinline__ void load_cols(const float* row, int64_t b, int64_t batch, float fill,
+                                          float (&v)[VEC]) {
+    if (VEC == 4 && b + 3 < batch) {
+        const float4 q = __ldg(reinterpret_cast<const float4*>(row + b));
+        v[0] = q.x;
+        v[VEC > 1 ? 1 : 0] = q.y;
+        v[VEC > 2 ? 2 : 0] = q.z;
+        v[VEC > 3 ? 3 : 0] = q.w;
+    } else {
+#pragma unroll
+        for (int u = 0; u < VEC; ++u) v[u] = b + u < batch ? __ldg(row + b + u) : fill;
+    }
+}
+
+template <int VEC>
+__device__ __forceinline__ void load_cols_hint(const float* row, int64_t b, int64_t batch,
+                                               float fill, uint64_t policy, float (&v)[VEC]) {
+    if (VEC == 4 && b + 3 < batch) {
+        asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.f32 {%0,%1,%2,%3}, [%4], %5;"
+                     : "=f"(v[0]), "=f"(v[VEC > 1 ? 1 : 0]), "=f"(v[VEC > 2 ? 2 : 0]),
+                       "=f"(v[VEC > 3 ? 3 : 0])
+                     : "l"(row + b), "l"(policy));
+    } else {
+#pragma unroll
+        for (int u = 0; u < VEC; ++u) v[u] = b + u < batch ? __ldg(row + b + u) : fill;
+    }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    return v;
+}
+
+// One warp per output row (k, p); columns in chunks of 32 * VEC * J, lane
+// columns (j*32 + lane)*VEC within a chunk (each j a coalesced warp access).
+template <int VEC, int J>
+__global__ void __launch_bounds__(kWarpsPerCta * 32) sparse_param_grad_kernel(SparseBwdArgs A) {
+    constexpr int64_t kCols = 32 * VEC * J;
+    const int lane = threadIdx.x & 31;
+    const int64_t r = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
+    if (r >= A.num_nblocks * A.block_size) return;
+    const int64_t k = r / A.block_size;
+    const int p = static_cast<int>(r % A.block_size);
+    const int64_t n = __ldg(A.nids + k) + p;
+    if (n < 0 || n >= A.num_nodes) {
+        if (lane == 0 && A.err) *A.err = 1;
+        return;
+    }
+    const float* grow = A.node_grads + n * A.batch;
+    const float* nrow = A.node_mars + n * A.batch;
+    for (int e0 = 0; e0 < A.E; e0 += 32) {
+        const int cnt = min(32, A.E - e0);
+        int64_t c_l = -1, q_l = -1;
+        if (lane < cnt) {
+            c_l = __ldg(A.cids + k * A.E + e0 + lane);
+            q_l = __ldg(A.pids + k * A.E + e0 + lane) + p;
+            if (!(c_l >= 0 && c_l < A.num_elements && q_l >= 0 && q_l < A.num_params)) {
+                if (A.err) *A.err = 1;
+                c_l = -1;
+            }
+        }
+        float mine = 0.0f;  // lane e: edge e0 + e summed over the batch
+        for (int64_t col0 = 0; col0 < A.batch; col0 += kCols) {
+            float g[J][VEC], nm[J][VEC];
+#pragma unroll
+            for (int j = 0; j < J; ++j) {
+                const int64_t b = col0 + ((int64_t)j * 32 + lane) * VEC;
+                load_cols<VEC>(grow, b, A.batch, 0.0f, g[j]);
+                load_cols<VEC>(nrow, b, A.batch, -INFINITY, nm[j]);
+#pragma unroll
+                for (int u = 0; u < VEC; ++u)
+                    if (nm[j][u] == -INFINITY) g[j][u] = 0.0f;  // an impossible node passes nothing
+            }
+            for (int t = 0; t < cnt; t += kEdgesInFlight) {
+                float x[kEdgesInFlight][J][VEC];
+                int64_t c[kEdgesInFlight];
+#pragma unroll
+                for (int f = 0; f < kEdgesInFlight; ++f) {
+                    c[f] = __shfl_sync(0xffffffffu, c_l, (t + f) & 31);
+                    if (t + f < cnt && c[f] >= 0) {
+#pragma unroll
+                        for (int j = 0; j < J; ++j)
+                            load_cols<VEC>(A.em + c[f] * A.batch, col0 + ((int64_t)j * 32 + lane) * VEC,
+                                           A.batch, -INFINITY, x[f][j]);
+                    }
+                }
+#pragma unroll
+                for (int f = 0; f < kEdgesInFlight; ++f) {
+                    float part = 0.0f;
+                    if (t + f < cnt && c[f] >= 0) {
+#pragma unroll
+                        for (int j = 0; j < J; ++j)
+#pragma unroll
+                            for (int u = 0; u < VEC; ++u)
+                                if (g[j][u] != 0.0f) part += g[j][u] * exp_from(x[f][j][u], nm[j][u]);
+                    }
+                    part = warp_sum(part);
+                    if (lane == t + f) mine += part;
+                }
+            }
+        }
+        if (c_l >= 0 && __ldg(A.params + q_l) > 1e-45f) atomicAdd(A.param_grads + q_l, mine);
+    }
+}
+
+// One warp per (group of TPW column tiles of 32 * VEC columns, element row c),
+// group-major.
+template <int VEC, int TPW>
+__global__ void __launch_bounds__(kWarpsPerCta * 32) sparse_element_grad_kernel(SparseBwdArgs A) {
+    constexpr int PIF = 8 / TPW;  // parents in flight
+    const int lane = threadIdx.x & 31;
+    const int64_t w = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
+    const int64_t group = w / A.num_elements;
+    const int64_t c = w % A.num_elements;
+    const int64_t g0 = group * TPW * 32 * VEC;  // first column of the group
+    if (g0 >= A.batch) return;
+    // a malformed index never reads outside the unit arrays
+    const int64_t q0 = max((int64_t)0, __ldg(A.child_ptr + c));
+    const int64_t q1 = min(A.num_units, __ldg(A.child_ptr + c + 1));
+    if (q0 >= q1) return;
+    const uint64_t policy = evict_last_policy();
+    float x[TPW][VEC], acc[TPW][VEC];
+#pragma unroll
+    for (int t = 0; t < TPW; ++t) {
+        const int64_t b = g0 + ((int64_t)t * 32 + lane) * VEC;
+#pragma unroll
+        for (int u = 0; u < VEC; ++u) {
+            x[t][u] = b + u < A.batch ? __ldcs(A.em + c * A.batch + b + u) : -INFINITY;
+            acc[t][u] = 0.0f;
+        }
+    }
+    for (int64_t u0 = q0; u0 < q1; u0 += 32) {
+        const int cnt = static_cast<int>(min((int64_t)32, q1 - u0));
+        int64_t n_l = -1;
+        float lw_l = 0.0f;
+        if (lane < cnt) {
+            const int64_t n = __ldg(A.unit_node + u0 + lane);
+            const int64_t q = __ldg(A.unit_param + u0 + lane);
+            if (n >= 0 && n < A.num_nodes && q >= 0 && q < A.num_params) {
+                n_l = n;
+                lw_l = log_weight(__ldg(A.params + q));
+            } else if (A.err) {
+                *A.err = 1;
+            }
+        }
+        for (int i = 0; i < cnt; i += PIF) {
+            float gv[PIF][TPW][VEC], nv[PIF][TPW][VEC];
+            int64_t n[PIF];
+            float lw[PIF];
+#pragma unroll
+            for (int f = 0; f < PIF; ++f) {
+                n[f] = __shfl_sync(0xffffffffu, n_l, (i + f) & 31);
+                lw[f] = __shfl_sync(0xffffffffu, lw_l, (i + f) & 31);
+                if (i + f < cnt && n[f] >= 0) {
+#pragma unroll
+                    for (int t = 0; t < TPW; ++t) {
+                        const int64_t b = g0 + ((int64_t)t * 32 + lane) * VEC;
+                        load_cols_hint<VEC>(A.node_grads + n[f] * A.batch, b, A.batch, 0.0f, policy, gv[f][t]);
+                        load_cols_hint<VEC>(A.node_mars + n[f] * A.batch, b, A.batch, -INFINITY, policy,
+                                            nv[f][t]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int f = 0; f < PIF; ++f) {
+                if (!(i + f < cnt && n[f] >= 0)) continue;
+#pragma unroll
+                for (int t = 0; t < TPW; ++t)
+#pragma unroll
+                    for (int u = 0; u < VEC; ++u)
+                        if (nv[f][t][u] != -INFINITY)
+                            acc[t][u] += gv[f][t][u] * exp_from(lw[f] + x[t][u], nv[f][t][u]);
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < TPW; ++t) {
+        const int64_t b = g0 + ((int64_t)t * 32 + lane) * VEC;
+        float* out = A.em_grads + c * A.batch + b;
+        if (VEC == 4 && b + 3 < A.batch) {
+            float4 v = __ldcs(reinterpret_cast<const float4*>(out));
+            v.x += acc[t][0];
+            v.y += acc[t][VEC > 1 ? 1 : 0];
+            v.z += acc[t][VEC > 2 ? 2 : 0];
+            v.w += acc[t][VEC > 3 ? 3 : 0];
+            __stcs(reinterpret_cast<float4*>(out), v);
+        } else {
+#pragma unroll
+            for (int u = 0; u < VEC; ++u)
+                if (b + u < A.batch) out[u] += acc[t][u];
+        }
+    }
+}
+
+template <int VEC, int J>
+int launch_cfg(const SparseBwdArgs& a, cudaStream_t s, const char* what) {
+    const int64_t rows = a.num_nblocks * a.block_size;
+    if (a.param_grads && rows > 0) {
+        const int64_t grid = (rows + kWarpsPerCta - 1) / kWarpsPerCta;
+        FL_REQUIRE(grid <= INT32_MAX, "%s: too many rows", what);
+        sparse_param_grad_kernel<VEC, J><<<(unsigned)grid, kWarpsPerCta * 32, 0, s>>>(a);
+    }
+    if (a.em_grads && a.num_elements > 0) {
+        constexpr int TPW = FL_SPBWD_TILES_PER_WARP;
+        const int64_t groups = (a.batch + TPW * 32 * VEC - 1) / (TPW * 32 * VEC);
+        const int64_t grid = (a.num_elements * groups + kWarpsPerCta - 1) / kWarpsPerCta;
+        FL_REQUIRE(grid <= INT32_MAX, "%s: too many rows", what);
+        sparse_element_grad_kernel<VEC, TPW><<<(unsigned)grid, kWarpsPerCta * 32, 0, s>>>(a);
+    }
+    return FL_OK;
+}
+
+}  // namespace
+}  // namespace fl
+
+using namespace fl;
+
+extern "C" int fl_sparse_f32_bwd(const float* node_mars, const float* node_grads,
+                                 const float* element_mars, const float* params,
+                                 const int64_t* nids, const int64_t* cids, const int64_t* pids,
+                                 const int64_t* child_ptr, const int64_t* unit_node,
+                                 const int64_t* unit_param, int64_t num_units,
+                                 float* element_grads, float* param_grads, int64_t num_nodes,
+                                 int64_t num_elements, int64_t num_params, int64_t num_nblocks,
+                                 int64_t num_edges, int64_t batch, int64_t block_size,
+                                 int* err_flag, fl_stream_t stream) {
+    clear_error();
+    const char* what = "fl_sparse_f32_bwd";
+    FL_REQUIRE(num_nodes >= 0 && num_elements >= 0 && num_params >= 0 && num_nblocks >= 0 &&
+                   num_edges >= 0 && batch >= 0 && block_size >= 0 && num_units >= 0,
+               "%s: negative size", what);
+    FL_REQUIRE(num_edges <= INT32_MAX && block_size <= INT32_MAX, "%s: sizes too large", what);
+    if (batch == 0 || num_nblocks == 0 || block_size == 0 || num_edges == 0) return FL_OK;
+    if (!element_grads && !param_grads) return FL_OK;
+    FL_REQUIRE(node_mars && node_grads && element_mars && params && nids && cids && pids,
+               "%s: NULL buffer", what);
+    FL_REQUIRE(!element_grads || (child_ptr && (num_units == 0 || (unit_node && unit_param))),
+               "%s: element gradients need the child -> parent-unit index", what);
+    FL_REQUIRE(aligned_to(node_mars, 4) && aligned_to(node_grads, 4) && aligned_to(element_mars, 4) &&
+                   aligned_to(params, 4) && aligned_to(element_grads, 4) && aligned_to(param_grads, 4) &&
+                   aligned_to(nids, 8) && aligned_to(cids, 8) && aligned_to(pids, 8) &&
+                   aligned_to(child_ptr, 8) && aligned_to(unit_node, 8) && aligned_to(unit_param, 8),
+               "%s: misaligned buffer", what);
+    if (int st = bind_device(stream, element_grads ? (const void*)element_grads : param_grads))
+        return st;
+    SparseBwdArgs a{node_mars, node_grads, element_mars, params, nids, cids, pids, child_ptr,
+                    unit_node, unit_param, num_units, element_grads, param_grads, num_nodes,
+                    num_elements, num_params, num_nblocks, batch, static_cast<int>(num_edges),
+                    static_cast<int>(block_size), err_flag};
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    // 16-byte column groups when every row starts 16-byte aligned; parameter
+    // kernel column chunks of 256 (128 for narrow batches)
+    const bool vec4 = batch % 4 == 0 && aligned_to(node_mars, 16) && aligned_to(node_grads, 16) &&
+                      aligned_to(element_mars, 16) && aligned_to(element_grads, 16);
+    const int st = vec4 ? (batch > 128 ? launch_cfg<4, 2>(a, s, what) : launch_cfg<4, 1>(a, s, what))
+                        : launch_cfg<1, 4>(a, s, what);
+    if (st) return st;
+    return check_launch(what);
+}

@@ -17,7 +17,9 @@ Reference bindings replaced (file:line):
   sparse_forward_float              experiment_pyjuice/sparse_float_kernel.cu:110-172
   sparse_forward_q16                experiment_pyjuice/sparse_q16_kernel.cu:139-207
 Additions without a reference counterpart: batched_logsumexp_q16_i32,
-lse_partial, lse_combine, sparse_log_weights.
+lse_partial, lse_combine, sparse_log_weights, sparse_parent_index,
+sparse_backward_float, selective_logsoftmax_* (fused target gather + LSE),
+row_layout / *_strided (rows read in place) and logsumexp_dim* (dim != -1).
 """
 from __future__ import annotations
 
@@ -451,6 +453,76 @@ def sparse_forward_float(node_mars, element_mars, params, nids, cids, pids, bloc
 def sparse_forward_q16(node_mars, element_mars, params, nids, cids, pids, block_size) -> None:
     """Q16.16 version of sparse_forward_float, bit-identical to the reference kernel."""
     _sparse("fl_sparse_q16", node_mars, element_mars, params, nids, cids, pids, block_size)
+
+
+def sparse_parent_index(nids: torch.Tensor, cids: torch.Tensor, pids: torch.Tensor,
+                        block_size: int, num_elements: int):
+    """Child -> parent-unit index of a layer structure, built once:
+    (child_ptr, unit_node, unit_param).  The parent units of child c — one per
+    edge (k, e) with cids[k, e] = c and per p < block_size — are
+    [child_ptr[c], child_ptr[c+1]) of unit_node (node row nids[k] + p) and
+    unit_param (pids[k, e] + p), in edge order (a stable sort, so the backward
+    sums each child's parents in a fixed order).  Edges whose child is out of
+    range are left out."""
+    _check(cids.is_cuda and cids.dtype == torch.int64 and cids.dim() == 2, "cids must be CUDA int64 (K, E)")
+    _check(pids.shape == cids.shape and nids.dim() == 1 and nids.size(0) == cids.size(0),
+           "nids (K,), cids and pids (K, E) expected")
+    E = cids.size(1)
+    flat = cids.reshape(-1)
+    valid = (flat >= 0) & (flat < num_elements)
+    keys = torch.where(valid, flat, torch.full_like(flat, num_elements))
+    order = torch.argsort(keys, stable=True)
+    counts = torch.bincount(keys, minlength=num_elements + 1)[:num_elements] * block_size
+    child_ptr = torch.zeros(num_elements + 1, dtype=torch.int64, device=cids.device)
+    torch.cumsum(counts, 0, out=child_ptr[1:])
+    ar = torch.arange(block_size, device=cids.device, dtype=torch.int64)
+    unit_node = (nids[order // max(E, 1)][:, None] + ar[None, :]).reshape(-1).contiguous()
+    unit_param = (pids.reshape(-1)[order][:, None] + ar[None, :]).reshape(-1).contiguous()
+    return child_ptr, unit_node, unit_param
+
+
+def sparse_backward_float(node_mars, node_grads, element_mars, params, nids, cids, pids,
+                          block_size: int, element_grads=None, param_grads=None, parents=None,
+                          err_flag=None):
+    """Gradient of sparse_forward_float, added into element_grads (like
+    element_mars) and param_grads (like params); either may be None to skip it.
+    node_grads is d loss / d node_mars (only the layer's rows are read);
+    `parents` is sparse_parent_index(nids, cids, pids, block_size,
+    element_mars.size(0)), built here if None.  Returns (element_grads, param_grads)."""
+    for name, t, dt in (("node_mars", node_mars, torch.float32), ("node_grads", node_grads, torch.float32),
+                        ("element_mars", element_mars, torch.float32), ("params", params, torch.float32),
+                        ("nids", nids, torch.int64), ("cids", cids, torch.int64),
+                        ("pids", pids, torch.int64)):
+        _check(t.is_cuda and t.dtype == dt and t.is_contiguous(), f"{name} must be contiguous CUDA {dt}")
+        _check(t.device == node_mars.device, f"{name} must be on {node_mars.device}")
+    _check(node_grads.shape == node_mars.shape, "node_grads must match node_mars")
+    _check(cids.dim() == 2 and pids.shape == cids.shape and nids.dim() == 1 and
+           nids.size(0) == cids.size(0), "nids (K,), cids and pids (K, E) expected")
+    batch = node_mars.size(1)
+    _check(element_mars.size(1) == batch, "element_mars and node_mars batch sizes differ")
+    for name, t, like in (("element_grads", element_grads, element_mars), ("param_grads", param_grads, params)):
+        if t is not None:
+            _check(t.is_cuda and t.dtype == torch.float32 and t.is_contiguous() and t.shape == like.shape
+                   and t.device == node_mars.device,
+                   f"{name} must be a contiguous CUDA fp32 tensor shaped like {tuple(like.shape)}")
+    child_ptr = unit_node = unit_param = None
+    num_units = 0
+    if element_grads is not None:
+        if parents is None:
+            parents = sparse_parent_index(nids, cids, pids, block_size, element_mars.size(0))
+        child_ptr, unit_node, unit_param = parents
+        _check(child_ptr.numel() == element_mars.size(0) + 1 and unit_node.shape == unit_param.shape,
+               "parents index does not match this layer")
+        num_units = unit_node.numel()
+    num_nblocks, num_edges = cids.shape
+    ef = ptr(err_flag, ctypes.c_int) if err_flag is not None else None
+    call("fl_sparse_f32_bwd", ptr(node_mars), ptr(node_grads), ptr(element_mars), ptr(params),
+         ptr(nids, ctypes.c_int64), ptr(cids, ctypes.c_int64), ptr(pids, ctypes.c_int64),
+         ptr(child_ptr, ctypes.c_int64), ptr(unit_node, ctypes.c_int64),
+         ptr(unit_param, ctypes.c_int64), num_units, ptr(element_grads), ptr(param_grads),
+         node_mars.size(0), element_mars.size(0), params.numel(), num_nblocks, num_edges, batch,
+         int(block_size), ef, _stream(node_mars))
+    return element_grads, param_grads
 
 
 def sparse_log_weights(params: torch.Tensor) -> torch.Tensor:

@@ -272,6 +272,35 @@ int fl_sparse_q16(float* node_mars, const float* element_mars,
 int fl_sparse_log_weights(const float* params, float* logw, int64_t n,
                           fl_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Sparse sum-layer backward (fp32), the gradient of fl_sparse_f32.  With
+ * G = node_grads (d loss / d node_mars, (num_nodes, batch)) and node_mars
+ * the forward's output, ADDS to the caller's buffers
+ *   element_grads[c, b] += sum over edges (k, e, p) with cids[k, e] = c of
+ *                          G[n, b] * exp(lw + element_mars[c, b] - node_mars[n, b])
+ *   param_grads[q]      += sum over edges with pids[k, e] + p = q and over b of
+ *                          G[n, b] * exp(element_mars[c, b] - node_mars[n, b])
+ * with n = nids[k] + p and lw = log(max(params[q], 1e-45)); a parameter at or
+ * below the clamp gets no gradient, a node whose node_mars is -inf passes
+ * none.  Either output may be NULL (not computed).  element_grads needs the
+ * child -> parent-unit index of the layer, built once per structure: the
+ * parent units (edge, p) of child c are [child_ptr[c], child_ptr[c+1]) of
+ * unit_node (their node rows nids[k] + p) and unit_param (pids[k, e] + p);
+ * num_units is the length of those two arrays.  Indices out of range are
+ * skipped and set *err_flag = 1 when given.  The reference has no backward
+ * (experiment_pyjuice/sparse_float_kernel.cu is forward only); no reference
+ * counterpart.
+ * ---------------------------------------------------------------------- */
+int fl_sparse_f32_bwd(const float* node_mars, const float* node_grads,
+                      const float* element_mars, const float* params,
+                      const int64_t* nids, const int64_t* cids, const int64_t* pids,
+                      const int64_t* child_ptr, const int64_t* unit_node,
+                      const int64_t* unit_param, int64_t num_units,
+                      float* element_grads, float* param_grads, int64_t num_nodes,
+                      int64_t num_elements, int64_t num_params, int64_t num_nblocks,
+                      int64_t num_edges, int64_t batch, int64_t block_size,
+                      int* err_flag, fl_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -192,6 +192,34 @@ def sparse_f64(node_mars, element_mars, params, nids, cids, pids, block_size, fl
 
 
 # ---------------------------------------------------------------- CPU baseline (C port)
+def sparse_bwd_f64(node_mars, node_grads, element_mars, params, nids, cids, pids, block_size,
+                   floor=1e-45):
+    """fp64 gradient of the sparse layer (the reference has a forward only):
+    element grads sum over edges G[n] * w * exp(em[c] - nm[n]) into row c,
+    param grads sum over the batch G[n] * exp(em[c] - nm[n]) into params[q]
+    (0 for weights at or below the floor); nodes with nm = -inf pass nothing."""
+    nm = np.asarray(node_mars, np.float64)
+    G = np.asarray(node_grads, np.float64)
+    em = np.asarray(element_mars, np.float64)
+    w = np.asarray(params, np.float64)
+    gem = np.zeros_like(em)
+    gw = np.zeros_like(w)
+    K, E = cids.shape
+    for p in range(block_size):
+        n = nids + p                                          # (K,)
+        q = pids + p                                          # (K, E)
+        lw = np.log(np.maximum(w[q], floor))                  # (K, E)
+        dead = np.isneginf(nm[n])                             # (K, batch)
+        Gn = np.where(dead, 0.0, G[n])
+        with np.errstate(invalid="ignore", over="ignore"):
+            d = em[cids] - np.where(dead, 0.0, nm[n])[:, None, :]  # (K, E, batch)
+            r = Gn[:, None, :] * np.exp(d)
+        r = np.where(Gn[:, None, :] == 0.0, 0.0, r)
+        np.add.at(gem, cids.reshape(-1), (np.exp(lw)[:, :, None] * r).reshape(K * E, -1))
+        np.add.at(gw, q.reshape(-1), np.where(w[q] > floor, r.sum(-1), 0.0).reshape(-1))
+    return gem, gw
+
+
 def fuselse_cpu_port(x: np.ndarray, threads: int = 1) -> np.ndarray:
     """Reference FuseLSE-CPU pair chain, restated in C; rows split over threads."""
     x = np.ascontiguousarray(x, np.float32)

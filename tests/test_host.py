@@ -151,3 +151,33 @@ def test_row_layout_cases():
     assert ext.row_layout(torch.zeros(4, 5, 6, 7)[:, ::2, ::2, :]) is None  # three levels
     assert ext.row_layout(x.transpose(1, 2)) is None                      # last dim not unit-stride
     assert ext.row_layout(torch.zeros(1, 1, 9)) == (1, 9, -1, 0, 9)
+
+
+# ---------------------------------------------------------------- sparse backward oracle
+def test_sparse_bwd_oracle_matches_torch_autograd_cpu():
+    """The fp64 gradient oracle against torch autograd of the layer formula
+    (run_pyjuice.py:90-119 with the 1e-45 floor), block_size 2, shared
+    children and one weight below the floor."""
+    rng = np.random.default_rng(0)
+    P, K, E, batch, bs = 40, 6, 5, 7, 2
+    em = rng.standard_normal((P, batch)) * 3 - 5
+    nm0 = np.zeros((K * bs + 3, batch))
+    nids = np.arange(K) * bs + 3
+    cids = rng.integers(0, P, size=(K, E))
+    pids = np.arange(K * E).reshape(K, E) * bs
+    params = rng.random(K * E * bs) + 0.05
+    params[4] = 1e-50
+    G = rng.standard_normal(nm0.shape)
+
+    em_t = torch.tensor(em, requires_grad=True)
+    w_t = torch.tensor(params, requires_grad=True)
+    n = torch.tensor((nids[:, None] + np.arange(bs)[None, :]).reshape(-1))
+    c = torch.tensor(np.repeat(cids[:, None, :], bs, axis=1).reshape(K * bs, E))
+    q = torch.tensor((pids[:, None, :] + np.arange(bs)[None, :, None]).reshape(K * bs, E))
+    out = torch.tensor(nm0).clone()
+    out[n] = torch.logsumexp(em_t[c] + w_t[q].clamp(min=1e-45).log().unsqueeze(-1), dim=1)
+    (out * torch.tensor(G)).sum().backward()
+    gem, gw = O.sparse_bwd_f64(out.detach().numpy(), G, em, params, nids, cids, pids, bs)
+    np.testing.assert_allclose(gem, em_t.grad.numpy(), rtol=1e-10, atol=1e-12)
+    np.testing.assert_allclose(gw, w_t.grad.numpy(), rtol=1e-10, atol=1e-12)
+    assert gw[4] == 0.0
