@@ -43,9 +43,11 @@ constexpr int kWarpsPerCta = 8;
 constexpr int kEdgesInFlight = 4;  // children's rows gathered per step (parameter kernel)
 
 // Column tiles (of 32 * VEC columns) per warp in the element kernel; 8 / TPW
-// parents are in flight per step.
+// parents are in flight per step.  Measured on B200 for the default layer
+// (P 262144, S 65536, E 32, batch 512): 1 -> 3.34 ms, 2 -> 2.50 ms,
+// 4 -> 3.46 ms for the whole backward.
 #ifndef FL_SPBWD_TILES_PER_WARP
-#define FL_SPBWD_TILES_PER_WARP 4
+#define FL_SPBWD_TILES_PER_WARP 2
 #endif
 
 __device__ __forceinline__ float log_weight(float w) { return __logf(fmaxf(w, 1e-45f)); }
