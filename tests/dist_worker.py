@@ -96,7 +96,16 @@ def main():
     xb = W.fp32_rows(1000, 20000, seed=5, device=dev)
     r0, r1 = D.local_rows(xb.size(0))
     gathered = D.batch_sharded_logsumexp(xb[r0:r1], gather=True)
-    assert torch.equal(gathered, ext.onepass_lse_float_robust(xb)), "batch-shard gather differs"
+    # fewer rows per rank can change the launch shape (rows split over a
+    # cluster), hence the float association: equal to rounding, not bit for bit
+    want_b = ext.onepass_lse_float_robust(xb)
+    err = ((gathered - want_b).abs() / want_b.abs().clamp_min(1.0)).max().item()
+    assert err <= 1e-5, f"batch-shard gather err {err}"
+    # IntLSE's reduction order is fixed per row, so sharded rows are bit-exact
+    _, qb, _ = W.intlse_inputs(256, 40000, seed=6, device=dev)
+    r0, r1 = D.local_rows(qb.size(0))
+    got_q = D.batch_sharded_logsumexp(qb[r0:r1], gather=True, lse_fn=ext.batched_logsumexp_q16_i32)
+    assert torch.equal(got_q, ext.batched_logsumexp_q16_i32(qb)), "IntLSE batch shards differ"
     dist.barrier()
     if dist.get_rank() == 0:
         print(f"dist ok: world {G}", flush=True)

@@ -29,5 +29,7 @@ def test_sharded_paths_match_single_gpu(world):
            "--master-port", str(_port()), str(ROOT / "tests" / "dist_worker.py")]
     r = subprocess.run(cmd, capture_output=True, text=True, cwd=ROOT,
                        env=dict(os.environ, NCCL_NVLS_ENABLE="0"))
-    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    # the workers' own error lines first (torchrun's summary follows them)
+    errors = [l for l in r.stderr.splitlines() if "Error" in l and "elastic" not in l]
+    assert r.returncode == 0, "\n".join(errors[:20]) + "\n" + r.stdout[-2000:] + r.stderr[-2000:]
     assert f"dist ok: world {world}" in r.stdout
