@@ -29,7 +29,7 @@
 //     coalesced load and one load of their weights); a warp covers a group of
 //     TPW column tiles of one child, groups ordered group-major so the group's
 //     slice of the parents' G and nm rows stays in L2 (evict-last) while the
-//     element rows stream (evict-first); 8 / TPW parents' rows in flight; the
+//     element rows stream (evict-first); PIF parents' rows in flight; the
 //     sum is formed in registers and added once: no float atomics and a fixed
 //     order, so the result is deterministic.
 #include "common.cuh"
@@ -42,12 +42,21 @@ namespace {
 constexpr int kWarpsPerCta = 8;
 constexpr int kEdgesInFlight = 4;  // children's rows gathered per step (parameter kernel)
 
-// Column tiles (of 32 * VEC columns) per warp in the element kernel; 8 / TPW
-// parents are in flight per step.  Measured on B200 for the default layer
-// (P 262144, S 65536, E 32, batch 512): 1 -> 3.34 ms, 2 -> 2.50 ms,
-// 4 -> 3.46 ms for the whole backward.
+// Element kernel shape: column tiles (of 32 * VEC columns) per warp, parents
+// whose rows are in flight per step, and the minimum resident CTAs per SM
+// asked of the compiler (a register cap).  Measured on B200 for the default
+// layer (P 262144, S 65536, E 32, batch 512), whole backward: tiles 1 / 2 / 4
+// with 8 / 4 / 2 parents in flight -> 3.34 / 2.50 / 3.46 ms; 2 tiles with 2
+// parents and 3 CTAs per SM (80 registers) -> 2.35 ms; a 3-CTA cap on 4
+// parents spills (2.81 ms).
 #ifndef FL_SPBWD_TILES_PER_WARP
 #define FL_SPBWD_TILES_PER_WARP 2
+#endif
+#ifndef FL_SPBWD_PIF
+#define FL_SPBWD_PIF 2
+#endif
+#ifndef FL_SPBWD_MIN_BLOCKS
+#define FL_SPBWD_MIN_BLOCKS 3
 #endif
 
 __device__ __forceinline__ float log_weight(float w) { return __logf(fmaxf(w, 1e-45f)); }
@@ -189,8 +198,9 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) sparse_param_grad_kernel(Sp
 // One warp per (group of TPW column tiles of 32 * VEC columns, element row c),
 // group-major.
 template <int VEC, int TPW>
-__global__ void __launch_bounds__(kWarpsPerCta * 32) sparse_element_grad_kernel(SparseBwdArgs A) {
-    constexpr int PIF = 8 / TPW;  // parents in flight
+__global__ void __launch_bounds__(kWarpsPerCta * 32, FL_SPBWD_MIN_BLOCKS)
+    sparse_element_grad_kernel(SparseBwdArgs A) {
+    constexpr int PIF = FL_SPBWD_PIF;  // parents in flight
     const int lane = threadIdx.x & 31;
     const int64_t w = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
     const int64_t group = w / A.num_elements;
