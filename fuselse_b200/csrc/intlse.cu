@@ -26,6 +26,8 @@
 
 #include <cooperative_groups.h>
 
+#include <algorithm>
+
 namespace cg = cooperative_groups;
 
 namespace fl {
@@ -47,6 +49,13 @@ enum Kind { kQ16F32 = 0, kQ16I32 = 1, kQ106I16 = 2 };
 #endif
 #ifndef FL_INTLSE_DMID
 #define FL_INTLSE_DMID 4
+#endif
+// One-CTA-per-row launches over rows of at most this many bytes use only the
+// resident CTAs, each looping over rows and filling its table once (measured
+// on B200, int32 input: (65536, 1024) 197 -> 177 us; for 16 KB rows the row
+// loop's barrier cost more than it saved, (16384, 4096) 81 -> 86 us).  0 = off.
+#ifndef FL_INTLSE_PERSIST_ROW_BYTES
+#define FL_INTLSE_PERSIST_ROW_BYTES 4096
 #endif
 
 // Reference constants (lse_kernel.cu:23-27): CONV = LOG2_E * 2^16 and
@@ -128,10 +137,12 @@ __device__ __forceinline__ float to_output(int acc) {
     return __fmul_rn(__int2float_rn(acc), F == 16 ? kOutQ16 : kOutQ106);
 }
 
-// CTA threads run the chains [rank*CTA, rank*CTA + CTA) of one row.
+// CTA threads run the chains [rank*CTA, rank*CTA + CTA) of one row.  With one
+// CTA per row (C == 1) the grid may be smaller than B: each CTA then takes
+// rows blockIdx.x, blockIdx.x + gridDim.x, ... and fills its table once.
 template <int KIND, bool LUT, int CTA, int D>
 __global__ void __launch_bounds__(CTA) intlse_rows_kernel(
-    const typename IK<KIND>::In* __restrict__ x, float* __restrict__ out, int64_t N) {
+    const typename IK<KIND>::In* __restrict__ x, float* __restrict__ out, int64_t B, int64_t N) {
     using In = typename IK<KIND>::In;
     constexpr int F = IK<KIND>::F;
     constexpr int C = 256 / CTA;
@@ -139,7 +150,6 @@ __global__ void __launch_bounds__(CTA) intlse_rows_kernel(
     __shared__ int warp_val[8];
 
     const int rank = C > 1 ? static_cast<int>(blockIdx.x % C) : 0;
-    const int64_t row = blockIdx.x / C;
     const int lane = threadIdx.x & 31;
     const int t = rank * CTA + threadIdx.x;
 
@@ -149,94 +159,98 @@ __global__ void __launch_bounds__(CTA) intlse_rows_kernel(
     }
     const LaneLut lut{lut_s, lane};
 
-    const In* rowp = x + row * N;
-    const int64_t head = head_count<KIND>(rowp, N);
-    const int64_t nv = (N - head) / 4;
-    const int64_t tail0 = head + nv * 4;
-    const In* vbase = rowp + head;
+    const int64_t row_step = gridDim.x / C;
+    for (int64_t row = blockIdx.x / C; row < B; row += row_step) {
+        const In* rowp = x + row * N;
+        const int64_t head = head_count<KIND>(rowp, N);
+        const int64_t nv = (N - head) / 4;
+        const int64_t tail0 = head + nv * 4;
+        const In* vbase = rowp + head;
 
-    int acc = kQNegInf;
-    bool has = false;
-    if (t < head) {
-        acc = IK<KIND>::load1(rowp + t);
-        has = true;
-    }
-    // vector step 0 carries the seed when there was no head element
-    if (t < nv) {
-        const Q4 q = load_vec_at<KIND>(vbase + 4 * (int64_t)t);
-        acc = has ? pair_exact<F, LUT>(acc, q.v[0], lut) : q.v[0];
-        has = true;
-#pragma unroll
-        for (int e = 1; e < 4; ++e) acc = pair_exact<F, LUT>(acc, q.v[e], lut);
-    }
-    // Round k holds vectors k*256 .. k*256+255; chain t takes vector k*256 + t.
-    // Rounds 1 .. Kf-1 are full (every chain has a vector, and a seed from
-    // round 0); round Kf is partial when 256 does not divide nv.  The full
-    // rounds run predicate-free with D rounds of loads in flight per chain.
-    const int64_t Kf = nv / 256;
-    const In* p = vbase + 4 * (int64_t)t;  // chain t's vector in round 0
-    constexpr int64_t kRound = 4 * 256;    // elements per round
-    {
-        Q4 buf[D];
-#pragma unroll
-        for (int d = 0; d < D; ++d)
-            if (1 + d < Kf) buf[d] = load_vec_at<KIND>(p + (1 + d) * kRound);
-        int64_t k = 1;
-        for (; k + 2 * D <= Kf; k += D) {  // every load of the block is a full round
-#pragma unroll
-            for (int d = 0; d < D; ++d) {
-                const Q4 cur = buf[d];
-                buf[d] = load_vec_at<KIND>(p + (k + d + D) * kRound);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) acc = pair_exact<F, LUT>(acc, cur.v[e], lut);
-            }
+        int acc = kQNegInf;
+        bool has = false;
+        if (t < head) {
+            acc = IK<KIND>::load1(rowp + t);
+            has = true;
         }
-        for (; k < Kf; k += D) {  // the last (< 2D) full rounds
+        // vector step 0 carries the seed when there was no head element
+        if (t < nv) {
+            const Q4 q = load_vec_at<KIND>(vbase + 4 * (int64_t)t);
+            acc = has ? pair_exact<F, LUT>(acc, q.v[0], lut) : q.v[0];
+            has = true;
 #pragma unroll
-            for (int d = 0; d < D; ++d) {
-                if (k + d < Kf) {
+            for (int e = 1; e < 4; ++e) acc = pair_exact<F, LUT>(acc, q.v[e], lut);
+        }
+        // Round k holds vectors k*256 .. k*256+255; chain t takes vector k*256 + t.
+        // Rounds 1 .. Kf-1 are full (every chain has a vector, and a seed from
+        // round 0); round Kf is partial when 256 does not divide nv.  The full
+        // rounds run predicate-free with D rounds of loads in flight per chain.
+        const int64_t Kf = nv / 256;
+        const In* p = vbase + 4 * (int64_t)t;  // chain t's vector in round 0
+        constexpr int64_t kRound = 4 * 256;    // elements per round
+        {
+            Q4 buf[D];
+#pragma unroll
+            for (int d = 0; d < D; ++d)
+                if (1 + d < Kf) buf[d] = load_vec_at<KIND>(p + (1 + d) * kRound);
+            int64_t k = 1;
+            for (; k + 2 * D <= Kf; k += D) {  // every load of the block is a full round
+#pragma unroll
+                for (int d = 0; d < D; ++d) {
                     const Q4 cur = buf[d];
-                    if (k + d + D < Kf) buf[d] = load_vec_at<KIND>(p + (k + d + D) * kRound);
+                    buf[d] = load_vec_at<KIND>(p + (k + d + D) * kRound);
 #pragma unroll
                     for (int e = 0; e < 4; ++e) acc = pair_exact<F, LUT>(acc, cur.v[e], lut);
                 }
             }
-        }
-    }
-    if (Kf >= 1 && Kf * 256 + t < nv) {  // partial round (round 0 was handled above)
-        const Q4 cur = load_vec_at<KIND>(p + Kf * kRound);
+            for (; k < Kf; k += D) {  // the last (< 2D) full rounds
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc = pair_exact<F, LUT>(acc, cur.v[e], lut);
-    }
-    if (tail0 + t < N) {
-        const int q = IK<KIND>::load1(rowp + tail0 + t);
-        acc = has ? pair_exact<F, LUT>(acc, q, lut) : q;
-    }
-
-    // warp butterfly (reference lse_kernel.cu:116-119)
+                for (int d = 0; d < D; ++d) {
+                    if (k + d < Kf) {
+                        const Q4 cur = buf[d];
+                        if (k + d + D < Kf) buf[d] = load_vec_at<KIND>(p + (k + d + D) * kRound);
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1)
-        acc = pair_exact<F, LUT>(acc, __shfl_xor_sync(0xffffffffu, acc, off), lut);
-
-    if constexpr (C > 1) {
-        cg::cluster_group cluster = cg::this_cluster();
-        if (lane == 0) {
-            int* dst = cluster.map_shared_rank(warp_val, 0);
-            dst[t >> 5] = acc;
+                        for (int e = 0; e < 4; ++e) acc = pair_exact<F, LUT>(acc, cur.v[e], lut);
+                    }
+                }
+            }
         }
-        cluster.sync();
-        if (rank != 0) return;
-    } else {
-        if (lane == 0) warp_val[t >> 5] = acc;
-        __syncthreads();
-    }
-    // second butterfly over the 8 warp values padded to 32 lanes (:122-132)
-    if (threadIdx.x < 32) {
-        int v = lane < 8 ? warp_val[lane] : kQNegInf;
+        if (Kf >= 1 && Kf * 256 + t < nv) {  // partial round (round 0 was handled above)
+            const Q4 cur = load_vec_at<KIND>(p + Kf * kRound);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc = pair_exact<F, LUT>(acc, cur.v[e], lut);
+        }
+        if (tail0 + t < N) {
+            const int q = IK<KIND>::load1(rowp + tail0 + t);
+            acc = has ? pair_exact<F, LUT>(acc, q, lut) : q;
+        }
+
+        // warp butterfly (reference lse_kernel.cu:116-119)
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1)
-            v = pair_exact<F, LUT>(v, __shfl_xor_sync(0xffffffffu, v, off), lut);
-        if (lane == 0) out[row] = to_output<F>(v);
+            acc = pair_exact<F, LUT>(acc, __shfl_xor_sync(0xffffffffu, acc, off), lut);
+
+        if constexpr (C > 1) {
+            cg::cluster_group cluster = cg::this_cluster();
+            if (lane == 0) {
+                int* dst = cluster.map_shared_rank(warp_val, 0);
+                dst[t >> 5] = acc;
+            }
+            cluster.sync();
+            if (rank != 0) return;
+        } else {
+            if (lane == 0) warp_val[t >> 5] = acc;
+            __syncthreads();
+        }
+        // second butterfly over the 8 warp values padded to 32 lanes (:122-132)
+        if (threadIdx.x < 32) {
+            int v = lane < 8 ? warp_val[lane] : kQNegInf;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1)
+                v = pair_exact<F, LUT>(v, __shfl_xor_sync(0xffffffffu, v, off), lut);
+            if (lane == 0) out[row] = to_output<F>(v);
+        }
+        if constexpr (C == 1) __syncthreads();  // warp_val is rewritten by the next row
     }
 }
 
@@ -244,8 +258,19 @@ template <int KIND, bool LUT, int CTA, int D>
 int launch_cfg(const typename IK<KIND>::In* x, float* out, int64_t B, int64_t N,
                cudaStream_t stream) {
     constexpr int C = 256 / CTA;
+    int64_t grid = B * C;
+    if (C == 1 && N * (int64_t)sizeof(typename IK<KIND>::In) <= FL_INTLSE_PERSIST_ROW_BYTES) {
+        // rows beyond the resident CTAs go to the same CTAs in turn
+        static int per_sm = 0;
+        if (per_sm == 0) {
+            FL_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                &per_sm, intlse_rows_kernel<KIND, LUT, CTA, D>, CTA, 0));
+            if (per_sm < 1) per_sm = 1;
+        }
+        grid = std::min<int64_t>(grid, (int64_t)per_sm * sm_count());
+    }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(B * C));
+    cfg.gridDim = dim3((unsigned)grid);
     cfg.blockDim = dim3(CTA);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -255,7 +280,7 @@ int launch_cfg(const typename IK<KIND>::In* x, float* out, int64_t B, int64_t N,
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    FL_CUDA(cudaLaunchKernelEx(&cfg, intlse_rows_kernel<KIND, LUT, CTA, D>, x, out, N));
+    FL_CUDA(cudaLaunchKernelEx(&cfg, intlse_rows_kernel<KIND, LUT, CTA, D>, x, out, B, N));
     return FL_OK;
 }
 

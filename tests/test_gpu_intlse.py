@@ -146,3 +146,19 @@ def test_baseline_configs_vs_reference(ext, B, N):
     want, _ = O.intlse_rows(qi32[rows].cpu().numpy(), O.Q16_I32, True)
     np.testing.assert_array_equal(_bits(ext.batched_logsumexp_q16_i32(qi32[rows].contiguous())),
                                   want.view(np.int32))
+
+
+@pytest.mark.parametrize("B,N", [(5000, 1), (3000, 5), (4000, 256), (1000, 1023), (2000, 1024), (700, 1025)])
+@pytest.mark.parametrize("phase", [0, 3])
+def test_many_short_rows_all_kinds(ext, B, N, phase):
+    """Enough short rows that the one-CTA-per-row launch keeps only its
+    resident CTAs and loops each over rows (rows of <= 4 KB): bit for bit."""
+    x = _phased(_x(B, N, seed=B + N + phase, scale=3.0), phase)
+    want, _ = O.intlse_rows(x.cpu().numpy(), O.Q16_F32, True, base_phase=(phase * 4) % 16)
+    np.testing.assert_array_equal(_bits(ext.batched_logsumexp(x)), want.view(np.int32))
+    qi = _phased(torch.from_numpy(_q16_from_f32(x.cpu().numpy())).cuda(), phase)
+    want, _ = O.intlse_rows(qi.cpu().numpy(), O.Q16_I32, True, base_phase=(phase * 4) % 16)
+    np.testing.assert_array_equal(_bits(ext.batched_logsumexp_q16_i32(qi)), want.view(np.int32))
+    qs = _phased(torch.clamp(torch.round(x * 64), -32768, 32767).to(torch.int16), phase)
+    want, _ = O.intlse_rows(qs.cpu().numpy(), O.Q10_6_I16, True, base_phase=(phase * 2) % 16)
+    np.testing.assert_array_equal(_bits(ext.batched_logsumexp_q10_6(qs)), want.view(np.int32))
