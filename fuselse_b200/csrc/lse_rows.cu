@@ -11,10 +11,14 @@
 //     rows are split into `nseg` contiguous segments, one CTA each, the CTAs
 //     of a row forming a thread-block cluster whose partial states are merged
 //     through distributed shared memory (no global scratch, one launch);
-//   * short rows go one warp per row (8 rows per 256-thread CTA).
+//   * short rows go one warp per row (8 rows per 256-thread CTA);
+//   * output modes: lse, the (m, s) partial state of a vocab shard, or the
+//     selective log-softmax (lse and x[row, index[row]] - lse in the same pass);
+//   * rows may be strided in two levels (RowMap): slices read in place.
 // Backward (replaces logsumexp_float_backward_kernel, fused_fp32_kernel.cu:135-150):
 //   row-chunked grid (no per-element division), 16-byte load + 16-byte
-//   evict-first store per 4 elements, exp as FFMA + EX2.
+//   evict-first store per 4 elements, exp as FADD + FMUL + EX2 of (x - lse);
+//   the selective variant adds the one-hot term at the target column.
 #include "common.cuh"
 #include "rows.cuh"
 
