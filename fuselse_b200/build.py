@@ -15,6 +15,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
@@ -45,25 +46,36 @@ def _stale(obj: Path, src: Path) -> bool:
     return any(p.stat().st_mtime > t for p in [src, *HEADERS])
 
 
+def _compile(cc: str, src: Path, obj: Path, verbose: bool, ptxas_info: bool):
+    cmd = [cc, *ARCH, *COMMON, *EXTRA.get(src.name, []), "-c", str(src), "-o", str(obj)]
+    if ptxas_info:
+        cmd.insert(1, "-Xptxas=-v")
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    return src, cmd, r
+
+
 def build(verbose: bool = False, ptxas_info: bool = False) -> Path:
     BUILD.mkdir(exist_ok=True)
     cc = nvcc()
-    objs = []
+    objs, todo = [], []
     for src in sorted(CSRC.glob("*.cu")):
         obj = BUILD / (src.stem + ".o")
         objs.append(obj)
-        if not _stale(obj, src) and not ptxas_info:
-            continue
-        cmd = [cc, *ARCH, *COMMON, *EXTRA.get(src.name, []), "-c", str(src), "-o", str(obj)]
-        if ptxas_info:
-            cmd.insert(1, "-Xptxas=-v")
-        if verbose:
-            print(" ".join(cmd), flush=True)
-        r = subprocess.run(cmd, capture_output=True, text=True)
-        if r.returncode != 0 or verbose or ptxas_info:
-            sys.stderr.write(r.stdout + r.stderr)
-        if r.returncode != 0:
-            raise RuntimeError(f"nvcc failed on {src.name}")
+        if _stale(obj, src) or ptxas_info:
+            todo.append((src, obj))
+    # the translation units are independent: compile them side by side
+    workers = max(1, min(len(todo), os.cpu_count() or 1))
+    failed = []
+    with ThreadPoolExecutor(max_workers=workers) as pool:
+        for src, cmd, r in pool.map(lambda t: _compile(cc, t[0], t[1], verbose, ptxas_info), todo):
+            if verbose:
+                print(" ".join(cmd), flush=True)
+            if r.returncode != 0 or verbose or ptxas_info:
+                sys.stderr.write(r.stdout + r.stderr)
+            if r.returncode != 0:
+                failed.append(src.name)
+    if failed:
+        raise RuntimeError(f"nvcc failed on {', '.join(failed)}")
     if not LIB.exists() or any(o.stat().st_mtime > LIB.stat().st_mtime for o in objs):
         tmp = LIB.with_suffix(".so.tmp")
         cmd = [cc, *ARCH, "-shared", "-Xcompiler", "-fPIC", "-o", str(tmp), *map(str, objs)]

@@ -93,11 +93,26 @@ def build_ref() -> bool:
     if not REF_SIMD_SO.exists():
         _run(["gcc", "-O3", "-fPIC", "-shared", "-mavx2", "-mfma",
               str(REF_SRC / "intlse/cpu/lse_kernel_simd.c"), "-o", str(REF_SIMD_SO), "-lm"])
-    for name, rel in REF_CPU_EXT.items():
-        _build_torch_ext(name, REF_SRC / rel, cuda=False)
-    for name, rel in REF_CUDA.items():
-        _build_torch_ext(name, REF_SRC / rel, cuda=True)
+    jobs = [(name, str(REF_SRC / rel), False) for name, rel in REF_CPU_EXT.items()]
+    jobs += [(name, str(REF_SRC / rel), True) for name, rel in REF_CUDA.items()]
+    jobs = [j for j in jobs if not ext_path(j[0]).exists()]
+    if len(jobs) <= 1:
+        for j in jobs:
+            _build_torch_ext(j[0], Path(j[1]), j[2])
+        return True
+    # independent extensions: one worker process each (spawned, so no CUDA or
+    # torch state is inherited), as many at a time as there are cores
+    import multiprocessing as mp
+    from concurrent.futures import ProcessPoolExecutor
+    workers = max(1, min(len(jobs), os.cpu_count() or 1))
+    with ProcessPoolExecutor(max_workers=workers, mp_context=mp.get_context("spawn")) as pool:
+        for f in [pool.submit(_build_torch_ext_job, *j) for j in jobs]:
+            f.result()
     return True
+
+
+def _build_torch_ext_job(name: str, src: str, cuda: bool) -> None:
+    _build_torch_ext(name, Path(src), cuda)
 
 
 if __name__ == "__main__":
