@@ -201,3 +201,23 @@ def test_full_rlhf_llama3_shape(ext):
     gx = ext.selective_logsoftmax_backward(torch.ones(R, device="cuda"), x, lse, t)
     assert gx.double().sum(dim=1).abs().max().item() <= 1e-4
     del gx
+
+
+@pytest.mark.parametrize("shape", [(2, 300, 32000), (1, 129, 50257)])
+def test_vs_reference_rlhf_composition(shape):
+    """Against the reference's own path for this caller: trl's gather minus
+    the reference kernel onepass_lse_float (built from
+    fuselse/gpu/fused_fp32_kernel.cu) per sequence, as run_rlhf.py:145-157
+    runs it with torch.logsumexp routed to that kernel."""
+    import fuselse_b200
+    from tests.conftest import ref_ext_or_skip
+    ref = ref_ext_or_skip("ref_fused_fp32")
+    B, T, V = shape
+    g = torch.Generator(device="cuda").manual_seed(V + T)
+    logits = torch.randn(B, T, V, generator=g, device="cuda") * 2
+    idx = torch.randint(0, V, (B, T), generator=g, device="cuda")
+    want = (torch.gather(logits, -1, idx.unsqueeze(-1)).squeeze(-1)
+            - torch.stack([ref.onepass_lse_float(seq) for seq in logits]))
+    got = fuselse_b200.selective_log_softmax(logits, idx, robust=False)
+    scale = torch.logsumexp(logits, -1).abs().clamp_min(1.0)
+    assert ((got - want).abs() / scale).max().item() <= RTOL
