@@ -6,7 +6,8 @@ distributed result against the single-GPU kernels on the full input:
     (max, sumexp) pairs + ext.lse_combine, fp16 logits of the LLM config shape
     (rows scaled down);
   * vocab shards through the library's NVLink exchange, forward and backward;
-  * batch rows: robust fp32 forward on the local rows, gathered.
+  * batch rows: robust fp32 forward on the local rows, gathered;
+  * sparse layer over batch-column shards (fp32 and Q16.16), gathered.
 Exits non-zero on any mismatch.
 """
 import os
@@ -106,6 +107,21 @@ def main():
     r0, r1 = D.local_rows(qb.size(0))
     got_q = D.batch_sharded_logsumexp(qb[r0:r1], gather=True, lse_fn=ext.batched_logsumexp_q16_i32)
     assert torch.equal(got_q, ext.batched_logsumexp_q16_i32(qb)), "IntLSE batch shards differ"
+    # sparse layer sharded over batch columns: each rank holds its own
+    # (P, batch/G) slice of element_mars; a column's result depends on that
+    # column alone, so the gathered columns equal the 1-GPU layer bit for bit
+    node, em, params, nids, cids, pids, bs = W.sparse_layer(P=20000, S=3000, E=32, batch=256,
+                                                            seed=7, device=dev)
+    c0, c1 = D.local_columns(em.size(1))
+    for fn in (ext.sparse_forward_float, ext.sparse_forward_q16):
+        full = node.clone()
+        fn(full, em, params, nids, cids, pids, bs)
+        mine = node[:, c0:c1].contiguous()
+        fn(mine, em[:, c0:c1].contiguous(), params, nids, cids, pids, bs)
+        parts = [torch.empty(node.size(0), hi - lo, device=dev)
+                 for lo, hi in (D.split_range(em.size(1), G, r) for r in range(G))]
+        dist.all_gather(parts, mine)
+        assert torch.equal(torch.cat(parts, dim=1), full), f"{fn.__name__}: batch-column shards differ"
     dist.barrier()
     if dist.get_rank() == 0:
         print(f"dist ok: world {G}", flush=True)
