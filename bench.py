@@ -1,7 +1,7 @@
 """Benchmark of the row log-sum-exp hot path on B200 (driver contract).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload fwdbwd_f32|fwd_f32|sls_f32|f16_vocab|intlse_q16|intlse_q10_6|sparse_f32|sparse_q16|sparse_fwdbwd_f32]
+                    [--workload NAME] [--eager] [--flush-l2] [--no-e2e] [--no-cpu-baseline]
 
 One JSON line on rank 0.  Default workload (the headline, BASELINE metric):
 FuseLSE fp32 forward + backward over (B, N) = (512, 128256), x ~ N(0, 1),
@@ -22,6 +22,19 @@ with inputs larger than L2 (x and gx are 262 MB each, L2 126 MB; each kernel
 pays the write-back of the previous kernel's dirty lines, as in a training
 loop); `--flush-l2` instead evicts L2 between steps outside the events; barrier and
 synchronize around the timed region; max over ranks.
+
+`e2e` (default workload): the same metric through the public host-buffer API
+(fuselse_b200.host.HostRowPipeline): every step x and g are copied in from
+pinned host memory and lse and the gradient copied back, in 64-row chunks
+whose uploads, kernels and downloads overlap on three streams; h2d/d2h bytes
+are those copies.
+
+Other workloads (`--workload`): fwd_f32 (forward alone); sls_f32 (fused
+selective log-softmax forward + backward over RLHF-shaped logits
+(4, 1023, 128256)); f16_vocab / f16_vocab_nccl (fp16 vocab shard of
+(8192, 128256), exchanged over NVLink by the library or by NCCL); intlse_q16 /
+intlse_q10_6 [_long] (IntLSE at (16384, 4096) / (64, 1048576)); sparse_f32 /
+sparse_q16 (the PC sum layer) and sparse_fwdbwd_f32 (its forward + backward).
 
 `--impl reference` times the reference's own CPU implementation of the path
 (FuseLSE-CPU, fuselse/cpu/fused_fp32_cpu.cpp, built from source into
