@@ -337,8 +337,9 @@ class Sparse(Workload):
 class SparseFwdBwd(Workload):
     """Sparse PC sum layer forward + backward (fp32) on the default layer:
     the forward kernel, then fl_sparse_f32_bwd (parameter gradients
-    node-major, element gradients child-major over the parent index built
-    once, outside the timed region) with a fixed upstream gradient."""
+    node-major; G and node_mars folded into one row per node; element
+    gradients child-major over the parent index, which is built once, outside
+    the timed region, like the workspace) with a fixed upstream gradient."""
     name = "sparse_fwdbwd_f32"
     dtype = "f32"
 
@@ -354,6 +355,8 @@ class SparseFwdBwd(Workload):
         self.G = torch.randn(node.shape, generator=g, device=dev)
         self.gem = torch.zeros_like(em)
         self.gw = torch.zeros_like(params)
+        self.ws = torch.empty(ext.sparse_bwd_workspace_bytes(*node.shape), dtype=torch.uint8,
+                              device=dev)
         self.fwd_bytes = P * batch * 4 + S * batch * 4 + S * E * (8 + 8 + 4) + S * 8
         # em read, em grads read + written, node rows and their grads read,
         # param grads read + written, the edges' cids/pids, nids, and the
@@ -362,7 +365,7 @@ class SparseFwdBwd(Workload):
                           + S * 8 + (P + 1) * 8)
         self.config = {"workload": f"sparse PC sum layer fp32 forward + backward: P={P}, S={S}, "
                                    f"E={E}, batch={batch}", "l2": "inputs larger than L2, steps back to back"}
-        self.launches_per_step = 3
+        self.launches_per_step = 4
 
     def _fwd(self):
         self.ext.sparse_forward_float(*self.args)
@@ -371,7 +374,7 @@ class SparseFwdBwd(Workload):
         node, em, params, nids, cids, pids, bs = self.args
         self.ext.sparse_backward_float(node, self.G, em, params, nids, cids, pids, bs,
                                        element_grads=self.gem, param_grads=self.gw,
-                                       parents=self.parents)
+                                       parents=self.parents, workspace=self.ws)
 
     def kernels(self):
         return [("sparse_f32", self._fwd, self.fwd_bytes), ("sparse_bwd", self._bwd, self.bwd_bytes)]

@@ -32,6 +32,11 @@
 //     element rows stream (evict-first); PIF parents' rows in flight; the
 //     sum is formed in registers and added once: no float atomics and a fixed
 //     order, so the result is deterministic.
+// With a workspace, a pre-pass first folds each layer row's G and nm into
+// one row r = nm - log|G| (+inf where the node passes nothing) and a bit
+// mask of G's signs, so that a parent's term is +-exp(lw + em - r): the
+// element kernel then gathers one row and one 32-bit word per 32 columns per
+// parent instead of two rows.
 #include "common.cuh"
 
 #include <algorithm>
@@ -78,7 +83,19 @@ struct SparseBwdArgs {
     int64_t num_nodes, num_elements, num_params, num_nblocks, batch;
     int E, block_size;
     int* err;
+    float* fold_rows;       // (num_nodes, batch): nm - log|G| of the layer's rows
+    uint32_t* fold_signs;   // (num_nodes, sign_words): bit b % 32 of word b / 32 = G[n, b] < 0
+    int64_t sign_words;
 };
+
+// Workspace of the folded element path: the rows, then (256-byte aligned) the sign words.
+inline int64_t fold_sign_words(int64_t batch) { return (batch + 31) / 32; }
+inline int64_t fold_signs_offset(int64_t num_nodes, int64_t batch) {
+    return (num_nodes * batch * (int64_t)sizeof(float) + 255) / 256 * 256;
+}
+inline int64_t fold_workspace_bytes(int64_t num_nodes, int64_t batch) {
+    return fold_signs_offset(num_nodes, batch) + num_nodes * fold_sign_words(batch) * 4;
+}
 
 // L2 policy for rows that are gathered repeatedly within a column range.
 __device__ __forceinline__ uint64_t evict_last_policy() {
@@ -195,9 +212,41 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) sparse_param_grad_kernel(Sp
     }
 }
 
+// One warp per layer row (k, p): r[n, b] = nm - log|G| (+inf where nm is
+// -inf or G is 0) and the sign words of G, 32 columns per warp access, U
+// accesses in flight.  Rows listed twice are written twice with the same values.
+__global__ void __launch_bounds__(kWarpsPerCta * 32) sparse_fold_kernel(SparseBwdArgs A) {
+    constexpr int U = 4;
+    const int lane = threadIdx.x & 31;
+    const int64_t r = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
+    if (r >= A.num_nblocks * A.block_size) return;
+    const int64_t n = __ldg(A.nids + r / A.block_size) + r % A.block_size;
+    if (n < 0 || n >= A.num_nodes) return;  // flagged by the parameter and element kernels
+    const float* grow = A.node_grads + n * A.batch;
+    const float* nrow = A.node_mars + n * A.batch;
+    float* out = A.fold_rows + n * A.batch;
+    uint32_t* signs = A.fold_signs + n * A.sign_words;
+    for (int64_t b0 = 0; b0 < A.batch; b0 += 32 * U) {
+        float g[U], m[U];
+#pragma unroll
+        for (int j = 0; j < U; ++j) {
+            const int64_t b = b0 + j * 32 + lane;
+            g[j] = b < A.batch ? __ldcs(grow + b) : 0.0f;
+            m[j] = b < A.batch ? __ldcs(nrow + b) : -INFINITY;
+        }
+#pragma unroll
+        for (int j = 0; j < U; ++j) {
+            const int64_t b = b0 + j * 32 + lane;
+            const uint32_t word = __ballot_sync(0xffffffffu, g[j] < 0.0f);
+            if (b < A.batch) out[b] = m[j] == -INFINITY ? INFINITY : m[j] - logf(fabsf(g[j]));
+            if (lane == 0 && b < A.batch) signs[(b0 >> 5) + j] = word;
+        }
+    }
+}
+
 // One warp per (group of TPW column tiles of 32 * VEC columns, element row c),
-// group-major.
-template <int VEC, int TPW>
+// group-major.  FOLD: parents' terms from the folded rows and sign words.
+template <int VEC, int TPW, bool FOLD>
 __global__ void __launch_bounds__(kWarpsPerCta * 32, FL_SPBWD_MIN_BLOCKS)
     sparse_element_grad_kernel(SparseBwdArgs A) {
     constexpr int PIF = FL_SPBWD_PIF;  // parents in flight
@@ -237,7 +286,9 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, FL_SPBWD_MIN_BLOCKS)
             }
         }
         for (int i = 0; i < cnt; i += PIF) {
-            float gv[PIF][TPW][VEC], nv[PIF][TPW][VEC];
+            // FOLD: gv holds r and sw the sign word; else gv holds G and nv nm
+            float gv[PIF][TPW][VEC], nv[PIF][TPW][FOLD ? 1 : VEC];
+            uint32_t sw[PIF][TPW];
             int64_t n[PIF];
             float lw[PIF];
 #pragma unroll
@@ -248,9 +299,16 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, FL_SPBWD_MIN_BLOCKS)
 #pragma unroll
                     for (int t = 0; t < TPW; ++t) {
                         const int64_t b = g0 + ((int64_t)t * 32 + lane) * VEC;
-                        load_cols_hint<VEC>(A.node_grads + n[f] * A.batch, b, A.batch, 0.0f, policy, gv[f][t]);
-                        load_cols_hint<VEC>(A.node_mars + n[f] * A.batch, b, A.batch, -INFINITY, policy,
-                                            nv[f][t]);
+                        if constexpr (FOLD) {
+                            load_cols_hint<VEC>(A.fold_rows + n[f] * A.batch, b, A.batch, INFINITY,
+                                                policy, gv[f][t]);
+                            sw[f][t] = b < A.batch ? __ldg(A.fold_signs + n[f] * A.sign_words + (b >> 5)) : 0u;
+                        } else {
+                            load_cols_hint<VEC>(A.node_grads + n[f] * A.batch, b, A.batch, 0.0f, policy,
+                                                gv[f][t]);
+                            load_cols_hint<VEC>(A.node_mars + n[f] * A.batch, b, A.batch, -INFINITY,
+                                                policy, nv[f][t]);
+                        }
                     }
                 }
             }
@@ -258,11 +316,21 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, FL_SPBWD_MIN_BLOCKS)
             for (int f = 0; f < PIF; ++f) {
                 if (!(i + f < cnt && n[f] >= 0)) continue;
 #pragma unroll
-                for (int t = 0; t < TPW; ++t)
+                for (int t = 0; t < TPW; ++t) {
+                    const int sh = static_cast<int>((g0 + ((int64_t)t * 32 + lane) * VEC) & 31);
 #pragma unroll
-                    for (int u = 0; u < VEC; ++u)
-                        if (nv[f][t][u] != -INFINITY)
+                    for (int u = 0; u < VEC; ++u) {
+                        if constexpr (FOLD) {
+                            if (gv[f][t][u] != INFINITY) {
+                                const uint32_t neg = ((sw[f][t] >> (sh + u)) & 1u) << 31;
+                                acc[t][u] += __uint_as_float(
+                                    __float_as_uint(exp_from(lw[f] + x[t][u], gv[f][t][u])) ^ neg);
+                            }
+                        } else if (nv[f][t][u] != -INFINITY) {
                             acc[t][u] += gv[f][t][u] * exp_from(lw[f] + x[t][u], nv[f][t][u]);
+                        }
+                    }
+                }
             }
         }
     }
@@ -298,7 +366,14 @@ int launch_cfg(const SparseBwdArgs& a, cudaStream_t s, const char* what) {
         const int64_t groups = (a.batch + TPW * 32 * VEC - 1) / (TPW * 32 * VEC);
         const int64_t grid = (a.num_elements * groups + kWarpsPerCta - 1) / kWarpsPerCta;
         FL_REQUIRE(grid <= INT32_MAX, "%s: too many rows", what);
-        sparse_element_grad_kernel<VEC, TPW><<<(unsigned)grid, kWarpsPerCta * 32, 0, s>>>(a);
+        if (a.fold_rows) {
+            const int64_t fgrid = (rows + kWarpsPerCta - 1) / kWarpsPerCta;
+            FL_REQUIRE(fgrid <= INT32_MAX, "%s: too many rows", what);
+            sparse_fold_kernel<<<(unsigned)fgrid, kWarpsPerCta * 32, 0, s>>>(a);
+            sparse_element_grad_kernel<VEC, TPW, true><<<(unsigned)grid, kWarpsPerCta * 32, 0, s>>>(a);
+        } else {
+            sparse_element_grad_kernel<VEC, TPW, false><<<(unsigned)grid, kWarpsPerCta * 32, 0, s>>>(a);
+        }
     }
     return FL_OK;
 }
@@ -308,6 +383,14 @@ int launch_cfg(const SparseBwdArgs& a, cudaStream_t s, const char* what) {
 
 using namespace fl;
 
+extern "C" int fl_sparse_f32_bwd_workspace(int64_t num_nodes, int64_t batch, int64_t* bytes) {
+    clear_error();
+    FL_REQUIRE(num_nodes >= 0 && batch >= 0 && bytes, "fl_sparse_f32_bwd_workspace: bad arguments");
+    FL_REQUIRE(num_nodes <= (INT64_MAX / 8) / (batch + 32), "fl_sparse_f32_bwd_workspace: too large");
+    *bytes = fold_workspace_bytes(num_nodes, batch);
+    return FL_OK;
+}
+
 extern "C" int fl_sparse_f32_bwd(const float* node_mars, const float* node_grads,
                                  const float* element_mars, const float* params,
                                  const int64_t* nids, const int64_t* cids, const int64_t* pids,
@@ -316,7 +399,8 @@ extern "C" int fl_sparse_f32_bwd(const float* node_mars, const float* node_grads
                                  float* element_grads, float* param_grads, int64_t num_nodes,
                                  int64_t num_elements, int64_t num_params, int64_t num_nblocks,
                                  int64_t num_edges, int64_t batch, int64_t block_size,
-                                 int* err_flag, fl_stream_t stream) {
+                                 void* workspace, int64_t workspace_bytes, int* err_flag,
+                                 fl_stream_t stream) {
     clear_error();
     const char* what = "fl_sparse_f32_bwd";
     FL_REQUIRE(num_nodes >= 0 && num_elements >= 0 && num_params >= 0 && num_nblocks >= 0 &&
@@ -332,14 +416,26 @@ extern "C" int fl_sparse_f32_bwd(const float* node_mars, const float* node_grads
     FL_REQUIRE(aligned_to(node_mars, 4) && aligned_to(node_grads, 4) && aligned_to(element_mars, 4) &&
                    aligned_to(params, 4) && aligned_to(element_grads, 4) && aligned_to(param_grads, 4) &&
                    aligned_to(nids, 8) && aligned_to(cids, 8) && aligned_to(pids, 8) &&
-                   aligned_to(child_ptr, 8) && aligned_to(unit_node, 8) && aligned_to(unit_param, 8),
+                   aligned_to(child_ptr, 8) && aligned_to(unit_node, 8) && aligned_to(unit_param, 8) &&
+                   aligned_to(workspace, 256),
                "%s: misaligned buffer", what);
+    const bool fold = element_grads && workspace;
+    FL_REQUIRE(!fold || (num_nodes <= (INT64_MAX / 8) / (batch + 32) &&
+                         workspace_bytes >= fold_workspace_bytes(num_nodes, batch)),
+               "%s: workspace of %lld bytes, %lld needed", what, (long long)workspace_bytes,
+               (long long)(fold ? fold_workspace_bytes(num_nodes, batch) : 0));
     if (int st = bind_device(stream, element_grads ? (const void*)element_grads : param_grads))
         return st;
     SparseBwdArgs a{node_mars, node_grads, element_mars, params, nids, cids, pids, child_ptr,
                     unit_node, unit_param, num_units, element_grads, param_grads, num_nodes,
                     num_elements, num_params, num_nblocks, batch, static_cast<int>(num_edges),
-                    static_cast<int>(block_size), err_flag};
+                    static_cast<int>(block_size), err_flag, nullptr, nullptr,
+                    fold_sign_words(batch)};
+    if (fold) {
+        a.fold_rows = static_cast<float*>(workspace);
+        a.fold_signs = reinterpret_cast<uint32_t*>(static_cast<char*>(workspace) +
+                                                   fold_signs_offset(num_nodes, batch));
+    }
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     // 16-byte column groups when every row starts 16-byte aligned; parameter
     // kernel column chunks of 256 (128 for narrow batches)

@@ -481,14 +481,25 @@ def sparse_parent_index(nids: torch.Tensor, cids: torch.Tensor, pids: torch.Tens
     return child_ptr, unit_node, unit_param
 
 
+def sparse_bwd_workspace_bytes(num_nodes: int, batch: int) -> int:
+    """Bytes of the workspace sparse_backward_float(..., fold=True) uses."""
+    nbytes = ctypes.c_int64()
+    call("fl_sparse_f32_bwd_workspace", int(num_nodes), int(batch), ctypes.byref(nbytes))
+    return nbytes.value
+
+
 def sparse_backward_float(node_mars, node_grads, element_mars, params, nids, cids, pids,
                           block_size: int, element_grads=None, param_grads=None, parents=None,
-                          err_flag=None):
+                          err_flag=None, fold: bool = True, workspace=None):
     """Gradient of sparse_forward_float, added into element_grads (like
     element_mars) and param_grads (like params); either may be None to skip it.
     node_grads is d loss / d node_mars (only the layer's rows are read);
     `parents` is sparse_parent_index(nids, cids, pids, block_size,
-    element_mars.size(0)), built here if None.  Returns (element_grads, param_grads)."""
+    element_mars.size(0)), built here if None.  fold=True (the default) first
+    folds G and node_mars into one row per node so the element gradients gather
+    half the bytes; its scratch is `workspace` (a CUDA uint8 tensor of at least
+    sparse_bwd_workspace_bytes(*node_mars.shape)), allocated here if None.
+    Returns (element_grads, param_grads)."""
     for name, t, dt in (("node_mars", node_mars, torch.float32), ("node_grads", node_grads, torch.float32),
                         ("element_mars", element_mars, torch.float32), ("params", params, torch.float32),
                         ("nids", nids, torch.int64), ("cids", cids, torch.int64),
@@ -515,13 +526,22 @@ def sparse_backward_float(node_mars, node_grads, element_mars, params, nids, cid
                "parents index does not match this layer")
         num_units = unit_node.numel()
     num_nblocks, num_edges = cids.shape
+    ws, ws_bytes = None, 0
+    if fold and element_grads is not None:
+        need = sparse_bwd_workspace_bytes(node_mars.size(0), batch)
+        if workspace is None:
+            workspace = torch.empty(need, dtype=torch.uint8, device=node_mars.device)
+        _check(workspace.is_cuda and workspace.dtype == torch.uint8 and workspace.is_contiguous()
+               and workspace.numel() >= need and workspace.device == node_mars.device,
+               f"workspace must be a contiguous CUDA uint8 tensor of >= {need} bytes")
+        ws, ws_bytes = ctypes.c_void_p(workspace.data_ptr()), workspace.numel()
     ef = ptr(err_flag, ctypes.c_int) if err_flag is not None else None
     call("fl_sparse_f32_bwd", ptr(node_mars), ptr(node_grads), ptr(element_mars), ptr(params),
          ptr(nids, ctypes.c_int64), ptr(cids, ctypes.c_int64), ptr(pids, ctypes.c_int64),
          ptr(child_ptr, ctypes.c_int64), ptr(unit_node, ctypes.c_int64),
          ptr(unit_param, ctypes.c_int64), num_units, ptr(element_grads), ptr(param_grads),
          node_mars.size(0), element_mars.size(0), params.numel(), num_nblocks, num_edges, batch,
-         int(block_size), ef, _stream(node_mars))
+         int(block_size), ws, ws_bytes, ef, _stream(node_mars))
     return element_grads, param_grads
 
 

@@ -287,7 +287,11 @@ int fl_sparse_log_weights(const float* params, float* logw, int64_t n,
  * parent units (edge, p) of child c are [child_ptr[c], child_ptr[c+1]) of
  * unit_node (their node rows nids[k] + p) and unit_param (pids[k, e] + p);
  * num_units is the length of those two arrays.  Indices out of range are
- * skipped and set *err_flag = 1 when given.  The reference has no backward
+ * skipped and set *err_flag = 1 when given.  workspace (256-byte aligned, at
+ * least fl_sparse_f32_bwd_workspace bytes, contents undefined on entry and
+ * exit) lets the element gradients fold each layer row's G and node_mars
+ * into one gathered row first; NULL gathers both rows per parent instead
+ * (same results to rounding).  The reference has no backward
  * (experiment_pyjuice/sparse_float_kernel.cu is forward only); no reference
  * counterpart.
  * ---------------------------------------------------------------------- */
@@ -299,7 +303,11 @@ int fl_sparse_f32_bwd(const float* node_mars, const float* node_grads,
                       float* element_grads, float* param_grads, int64_t num_nodes,
                       int64_t num_elements, int64_t num_params, int64_t num_nblocks,
                       int64_t num_edges, int64_t batch, int64_t block_size,
+                      void* workspace, int64_t workspace_bytes,
                       int* err_flag, fl_stream_t stream);
+
+/* Bytes of fl_sparse_f32_bwd's workspace for node_mars of (num_nodes, batch). */
+int fl_sparse_f32_bwd_workspace(int64_t num_nodes, int64_t batch, int64_t* bytes);
 
 #ifdef __cplusplus
 }

@@ -63,3 +63,21 @@ def test_library_is_sm100a_only():
         pytest.skip("cuobjdump unavailable")
     arches = set(re.findall(r"sm_(\d+a?)", r.stdout))
     assert arches == {"100a"}, arches
+
+
+def test_sparse_bwd_workspace_checks_without_gpu():
+    from fuselse_b200 import _lib
+    L = _lib.lib()
+    nbytes = ctypes.c_int64()
+    assert L.fl_sparse_f32_bwd_workspace(1000, 70, ctypes.byref(nbytes)) == _lib.FL_OK
+    # the folded rows, 256-byte aligned, then one sign word per 32 columns
+    assert nbytes.value == (1000 * 70 * 4 + 255) // 256 * 256 + 1000 * 3 * 4
+    assert L.fl_sparse_f32_bwd_workspace(-1, 70, ctypes.byref(nbytes)) == _lib.FL_ERR_INVALID_ARGUMENT
+    # a workspace below that size is refused before any CUDA call
+    fp = lambda a: ctypes.cast(ctypes.c_void_p(a), ctypes.POINTER(ctypes.c_float))
+    ip = lambda a: ctypes.cast(ctypes.c_void_p(a), ctypes.POINTER(ctypes.c_int64))
+    st = L.fl_sparse_f32_bwd(fp(256), fp(512), fp(768), fp(1024), ip(1280), ip(1536), ip(1792),
+                             ip(2048), ip(2304), ip(2560), 1, fp(2816), None, 1000, 10, 10, 1, 1,
+                             70, 1, ctypes.c_void_p(4096), 1024, None, None)
+    assert st == _lib.FL_ERR_INVALID_ARGUMENT
+    assert b"workspace" in L.fl_last_error()

@@ -30,24 +30,47 @@ def _close(got, want, what):
 CASES = [(1, 1, 1), (5, 3, 2), (8, 64, 1), (17, 100, 3), (32, 130, 1), (33, 512, 1), (64, 1000, 2)]
 
 
+@pytest.mark.parametrize("fold", [True, False], ids=["fold", "nofold"])
 @pytest.mark.parametrize("E,batch,bs", CASES)
-def test_sparse_bwd_vs_oracle(ext, E, batch, bs):
+def test_sparse_bwd_vs_oracle(ext, E, batch, bs, fold):
     node, em, params, nids, cids, pids = layer(E * 77 + batch, 300, 40, E, batch, bs,
                                                zero_w=0.02, neg_inf=0.02)
     node_d, em_d, w_d, nids_d, cids_d, pids_d = to_dev(node, em, params, nids, cids, pids)
     ext.sparse_forward_float(node_d, em_d, w_d, nids_d, cids_d, pids_d, bs)
     rng = np.random.default_rng(batch)
     G = rng.standard_normal(node.shape).astype(np.float32)
+    G[rng.random(node.shape) < 0.05] = 0.0  # zero upstream gradients fold to +inf rows
     G_d = torch.from_numpy(G).cuda()
     gem = torch.zeros_like(em_d)
     gw = torch.zeros_like(w_d)
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     ext.sparse_backward_float(node_d, G_d, em_d, w_d, nids_d, cids_d, pids_d, bs,
-                              element_grads=gem, param_grads=gw, err_flag=err)
+                              element_grads=gem, param_grads=gw, err_flag=err, fold=fold)
     assert int(err.item()) == 0
     want_em, want_w = O.sparse_bwd_f64(node_d.cpu().numpy(), G, em, params, nids, cids, pids, bs)
     _close(gem.cpu().numpy(), want_em, f"element grads E={E} batch={batch} bs={bs}")
     _close(gw.cpu().numpy(), want_w, f"param grads E={E} batch={batch} bs={bs}")
+
+
+def test_sparse_bwd_fold_workspace(ext):
+    """A caller-owned workspace (reused across calls, larger than needed)
+    gives the same element gradients as one allocated per call; one that is
+    too small is refused."""
+    node, em, params, nids, cids, pids = layer(13, 400, 50, 16, 96, 2)
+    t = to_dev(node, em, params, nids, cids, pids)
+    ext.sparse_forward_float(*t, 2)
+    G = torch.randn_like(t[0])
+    need = ext.sparse_bwd_workspace_bytes(*t[0].shape)
+    ws = torch.full((need + 4096,), 0xFF, dtype=torch.uint8, device="cuda")  # NaN-filled rows
+    outs = []
+    for w in (None, ws, ws):
+        gem = torch.zeros_like(t[1])
+        ext.sparse_backward_float(t[0], G, *t[1:], 2, element_grads=gem, workspace=w)
+        outs.append(gem)
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+    with pytest.raises(RuntimeError, match="workspace"):
+        ext.sparse_backward_float(t[0], G, *t[1:], 2, element_grads=torch.zeros_like(t[1]),
+                                  workspace=ws[:need - 1])
 
 
 def test_sparse_bwd_accumulates_and_skips(ext):
