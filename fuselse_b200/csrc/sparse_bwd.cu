@@ -33,10 +33,14 @@
 //     sum is formed in registers and added once: no float atomics and a fixed
 //     order, so the result is deterministic.
 // With a workspace, a pre-pass first folds each layer row's G and nm into
-// one row r = nm - log|G| (+inf where the node passes nothing) and a bit
-// mask of G's signs, so that a parent's term is +-exp(lw + em - r): the
-// element kernel then gathers one row and one 32-bit word per 32 columns per
-// parent instead of two rows.
+// one row r = (nm - log|G|) * log2(e) (+inf where the node passes nothing)
+// and a bit mask of G's signs, so that a parent's term is
+// +-2^(em * log2(e) + (lw * log2(e) - r)) (the product exact inside one
+// fused multiply-add), and the
+// element gradients run as persistent warps that gather one row and one
+// 32-bit word per 32 columns per parent (instead of two rows) and load the
+// next children's parent indices while the current child's rows are in
+// flight.
 #include "common.cuh"
 
 #include <algorithm>
@@ -63,6 +67,20 @@ constexpr int kEdgesInFlight = 4;  // children's rows gathered per step (paramet
 #ifndef FL_SPBWD_MIN_BLOCKS
 #define FL_SPBWD_MIN_BLOCKS 3
 #endif
+// The folded path (persistent, index-prefetching warps).  Measured on B200
+// for the same layer, element gradients alone: tiles 2 with 1 / 2 / 3 / 4
+// parents in flight at 2 CTAs per SM -> 1.56 / 1.41 / 1.34 / 1.64 ms; tiles 1
+// -> 1.68-1.99 ms; tiles 4 -> 1.80-2.02 ms; the non-persistent kernel on the
+// folded rows 1.69-2.13 ms and on G and nm 1.68 ms.
+#ifndef FL_SPBWD_PERSIST_TILES_PER_WARP
+#define FL_SPBWD_PERSIST_TILES_PER_WARP 2
+#endif
+#ifndef FL_SPBWD_PERSIST_PIF
+#define FL_SPBWD_PERSIST_PIF 3
+#endif
+#ifndef FL_SPBWD_PERSIST_MIN_BLOCKS
+#define FL_SPBWD_PERSIST_MIN_BLOCKS 2
+#endif
 
 __device__ __forceinline__ float log_weight(float w) { return __logf(fmaxf(w, 1e-45f)); }
 
@@ -83,7 +101,7 @@ struct SparseBwdArgs {
     int64_t num_nodes, num_elements, num_params, num_nblocks, batch;
     int E, block_size;
     int* err;
-    float* fold_rows;       // (num_nodes, batch): nm - log|G| of the layer's rows
+    float* fold_rows;       // (num_nodes, batch): (nm - log|G|) * log2(e) of the layer's rows
     uint32_t* fold_signs;   // (num_nodes, sign_words): bit b % 32 of word b / 32 = G[n, b] < 0
     int64_t sign_words;
 };
@@ -176,9 +194,13 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) sparse_param_grad_kernel(Sp
                 const int64_t b = col0 + ((int64_t)j * 32 + lane) * VEC;
                 load_cols<VEC>(grow, b, A.batch, 0.0f, g[j]);
                 load_cols<VEC>(nrow, b, A.batch, -INFINITY, nm[j]);
+                // nm * log2(e), reused for every edge of the chunk; an impossible
+                // node (nm = -inf) passes nothing: +inf gives 2^-inf = 0
 #pragma unroll
-                for (int u = 0; u < VEC; ++u)
-                    if (nm[j][u] == -INFINITY) g[j][u] = 0.0f;  // an impossible node passes nothing
+                for (int u = 0; u < VEC; ++u) {
+                    if (nm[j][u] == -INFINITY) g[j][u] = 0.0f;
+                    nm[j][u] = nm[j][u] == -INFINITY ? INFINITY : nm[j][u] * kLog2e;
+                }
             }
             for (int t = 0; t < cnt; t += kEdgesInFlight) {
                 float x[kEdgesInFlight][J][VEC];
@@ -201,7 +223,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) sparse_param_grad_kernel(Sp
                         for (int j = 0; j < J; ++j)
 #pragma unroll
                             for (int u = 0; u < VEC; ++u)
-                                if (g[j][u] != 0.0f) part += g[j][u] * exp_from(x[f][j][u], nm[j][u]);
+                                part = fmaf(g[j][u], ex2(fmaf(x[f][j][u], kLog2e, -nm[j][u])), part);
                     }
                     part = warp_sum(part);
                     if (lane == t + f) mine += part;
@@ -212,8 +234,8 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) sparse_param_grad_kernel(Sp
     }
 }
 
-// One warp per layer row (k, p): r[n, b] = nm - log|G| (+inf where nm is
-// -inf or G is 0) and the sign words of G, 32 columns per warp access, U
+// One warp per layer row (k, p): r[n, b] = (nm - log|G|) * log2(e) (+inf
+// where nm is -inf or G is 0) and the sign words of G, 32 columns per warp access, U
 // accesses in flight.  Rows listed twice are written twice with the same values.
 __global__ void __launch_bounds__(kWarpsPerCta * 32) sparse_fold_kernel(SparseBwdArgs A) {
     constexpr int U = 4;
@@ -238,15 +260,15 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) sparse_fold_kernel(SparseBw
         for (int j = 0; j < U; ++j) {
             const int64_t b = b0 + j * 32 + lane;
             const uint32_t word = __ballot_sync(0xffffffffu, g[j] < 0.0f);
-            if (b < A.batch) out[b] = m[j] == -INFINITY ? INFINITY : m[j] - logf(fabsf(g[j]));
+            if (b < A.batch) out[b] = m[j] == -INFINITY ? INFINITY : (m[j] - logf(fabsf(g[j]))) * kLog2e;
             if (lane == 0 && b < A.batch) signs[(b0 >> 5) + j] = word;
         }
     }
 }
 
 // One warp per (group of TPW column tiles of 32 * VEC columns, element row c),
-// group-major.  FOLD: parents' terms from the folded rows and sign words.
-template <int VEC, int TPW, bool FOLD>
+// group-major; parents' G and nm rows gathered directly.
+template <int VEC, int TPW>
 __global__ void __launch_bounds__(kWarpsPerCta * 32, FL_SPBWD_MIN_BLOCKS)
     sparse_element_grad_kernel(SparseBwdArgs A) {
     constexpr int PIF = FL_SPBWD_PIF;  // parents in flight
@@ -286,9 +308,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, FL_SPBWD_MIN_BLOCKS)
             }
         }
         for (int i = 0; i < cnt; i += PIF) {
-            // FOLD: gv holds r and sw the sign word; else gv holds G and nv nm
-            float gv[PIF][TPW][VEC], nv[PIF][TPW][FOLD ? 1 : VEC];
-            uint32_t sw[PIF][TPW];
+            float gv[PIF][TPW][VEC], nv[PIF][TPW][VEC];
             int64_t n[PIF];
             float lw[PIF];
 #pragma unroll
@@ -299,16 +319,9 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, FL_SPBWD_MIN_BLOCKS)
 #pragma unroll
                     for (int t = 0; t < TPW; ++t) {
                         const int64_t b = g0 + ((int64_t)t * 32 + lane) * VEC;
-                        if constexpr (FOLD) {
-                            load_cols_hint<VEC>(A.fold_rows + n[f] * A.batch, b, A.batch, INFINITY,
-                                                policy, gv[f][t]);
-                            sw[f][t] = b < A.batch ? __ldg(A.fold_signs + n[f] * A.sign_words + (b >> 5)) : 0u;
-                        } else {
-                            load_cols_hint<VEC>(A.node_grads + n[f] * A.batch, b, A.batch, 0.0f, policy,
-                                                gv[f][t]);
-                            load_cols_hint<VEC>(A.node_mars + n[f] * A.batch, b, A.batch, -INFINITY,
-                                                policy, nv[f][t]);
-                        }
+                        load_cols_hint<VEC>(A.node_grads + n[f] * A.batch, b, A.batch, 0.0f, policy, gv[f][t]);
+                        load_cols_hint<VEC>(A.node_mars + n[f] * A.batch, b, A.batch, -INFINITY, policy,
+                                            nv[f][t]);
                     }
                 }
             }
@@ -316,21 +329,11 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, FL_SPBWD_MIN_BLOCKS)
             for (int f = 0; f < PIF; ++f) {
                 if (!(i + f < cnt && n[f] >= 0)) continue;
 #pragma unroll
-                for (int t = 0; t < TPW; ++t) {
-                    const int sh = static_cast<int>((g0 + ((int64_t)t * 32 + lane) * VEC) & 31);
+                for (int t = 0; t < TPW; ++t)
 #pragma unroll
-                    for (int u = 0; u < VEC; ++u) {
-                        if constexpr (FOLD) {
-                            if (gv[f][t][u] != INFINITY) {
-                                const uint32_t neg = ((sw[f][t] >> (sh + u)) & 1u) << 31;
-                                acc[t][u] += __uint_as_float(
-                                    __float_as_uint(exp_from(lw[f] + x[t][u], gv[f][t][u])) ^ neg);
-                            }
-                        } else if (nv[f][t][u] != -INFINITY) {
+                    for (int u = 0; u < VEC; ++u)
+                        if (nv[f][t][u] != -INFINITY)
                             acc[t][u] += gv[f][t][u] * exp_from(lw[f] + x[t][u], nv[f][t][u]);
-                        }
-                    }
-                }
             }
         }
     }
@@ -353,6 +356,169 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, FL_SPBWD_MIN_BLOCKS)
     }
 }
 
+// Parent-unit range of an item's child (empty past the last item), clamped
+// so that a malformed index never reads outside the unit arrays.
+__device__ __forceinline__ void item_units(const SparseBwdArgs& A, int64_t item, int64_t num_items,
+                                           int64_t& q0, int64_t& q1) {
+    q0 = q1 = 0;
+    if (item < num_items) {
+        const int64_t c = item % A.num_elements;
+        q0 = max((int64_t)0, __ldg(A.child_ptr + c));
+        q1 = min(A.num_units, __ldg(A.child_ptr + c + 1));
+    }
+}
+
+// Lane's unit among the first 32 of [q0, q1): node row and parameter index.
+__device__ __forceinline__ void first_units(const SparseBwdArgs& A, int64_t q0, int64_t q1, int lane,
+                                            int64_t& n, int64_t& q) {
+    n = q = -1;
+    if (q0 + lane < q1) {
+        n = __ldg(A.unit_node + q0 + lane);
+        q = __ldg(A.unit_param + q0 + lane);
+    }
+}
+
+// The folded element kernel as persistent warps: warp w takes items w, w + W,
+// ... (item = group * num_elements + c, group-major as above).  While item i's
+// parent rows are in flight the warp already holds item i+1's unit range and
+// loads its first 32 units, and loads item i+2's range, so the index chain
+// (child_ptr -> units -> weight) overlaps the gathers instead of preceding
+// them; the weights are needed only for the arithmetic, so their loads
+// overlap the first gathers too.  The previous gradient values are read with
+// the element row, and each (c, column) is still summed by one warp in a
+// fixed order.
+template <int VEC, int TPW, int PIF>
+__global__ void __launch_bounds__(kWarpsPerCta * 32, FL_SPBWD_PERSIST_MIN_BLOCKS)
+    sparse_element_grad_persist_kernel(SparseBwdArgs A, int64_t num_items) {
+    const int lane = threadIdx.x & 31;
+    const int64_t W = (int64_t)gridDim.x * kWarpsPerCta;
+    int64_t item = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
+    if (item >= num_items) return;
+    const uint64_t policy = evict_last_policy();
+    int64_t q0, q1, nq0, nq1, n_l, p_l;
+    item_units(A, item, num_items, q0, q1);
+    first_units(A, q0, q1, lane, n_l, p_l);
+    item_units(A, item + W, num_items, nq0, nq1);
+    for (; item < num_items; item += W) {
+        const int64_t group = item / A.num_elements;
+        const int64_t c = item - group * A.num_elements;
+        const int64_t g0 = group * TPW * 32 * VEC;
+        float x[TPW][VEC], acc[TPW][VEC], old[TPW][VEC];
+#pragma unroll
+        for (int t = 0; t < TPW; ++t) {
+            const int64_t b = g0 + ((int64_t)t * 32 + lane) * VEC;
+#pragma unroll
+            for (int u = 0; u < VEC; ++u) {
+                const bool in = b + u < A.batch;
+                x[t][u] = in ? __ldcs(A.em + c * A.batch + b + u) : -INFINITY;
+                old[t][u] = in ? __ldcs(A.em_grads + c * A.batch + b + u) : 0.0f;
+                acc[t][u] = 0.0f;
+            }
+        }
+        // this item's first units (loaded during the previous item): check them
+        // and start their weight loads
+        float w_l = 0.0f;
+        if (q0 + lane < q1) {
+            if (n_l >= 0 && n_l < A.num_nodes && p_l >= 0 && p_l < A.num_params) {
+                w_l = __ldg(A.params + p_l);
+            } else {
+                if (A.err) *A.err = 1;
+                n_l = -1;
+            }
+        }
+        // prefetch: the next item's first units, the range of the one after it
+        int64_t nn_l, np_l, mq0, mq1;
+        first_units(A, nq0, nq1, lane, nn_l, np_l);
+        item_units(A, item + 2 * W, num_items, mq0, mq1);
+        for (int64_t u0 = q0; u0 < q1; u0 += 32) {
+            const int cnt = static_cast<int>(min((int64_t)32, q1 - u0));
+            if (u0 != q0) {  // a child with more than 32 parent units: the rest in turn
+                n_l = -1;
+                w_l = 0.0f;
+                if (lane < cnt) {
+                    const int64_t n = __ldg(A.unit_node + u0 + lane);
+                    const int64_t q = __ldg(A.unit_param + u0 + lane);
+                    if (n >= 0 && n < A.num_nodes && q >= 0 && q < A.num_params) {
+                        n_l = n;
+                        w_l = __ldg(A.params + q);
+                    } else if (A.err) {
+                        *A.err = 1;
+                    }
+                }
+            }
+            float lw_l = 0.0f;
+            for (int i = 0; i < cnt; i += PIF) {
+                float rv[PIF][TPW][VEC];
+                uint32_t sw[PIF][TPW];
+                int64_t n[PIF];
+#pragma unroll
+                for (int f = 0; f < PIF; ++f) {
+                    n[f] = __shfl_sync(0xffffffffu, n_l, (i + f) & 31);
+                    if (i + f < cnt && n[f] >= 0) {
+#pragma unroll
+                        for (int t = 0; t < TPW; ++t) {
+                            const int64_t b = g0 + ((int64_t)t * 32 + lane) * VEC;
+                            load_cols_hint<VEC>(A.fold_rows + n[f] * A.batch, b, A.batch, INFINITY,
+                                                policy, rv[f][t]);
+                            sw[f][t] = b < A.batch ? __ldg(A.fold_signs + n[f] * A.sign_words + (b >> 5)) : 0u;
+                        }
+                    }
+                }
+                // the weights arrived with the first rows
+                if (i == 0) lw_l = log_weight(w_l) * kLog2e;
+#pragma unroll
+                for (int f = 0; f < PIF; ++f) {
+                    const float lw = __shfl_sync(0xffffffffu, lw_l, (i + f) & 31);
+                    if (!(i + f < cnt && n[f] >= 0)) continue;
+#pragma unroll
+                    for (int t = 0; t < TPW; ++t) {
+                        // column b + u's sign bit moved to bit 32 - VEC + u
+                        const int sh = static_cast<int>((g0 + ((int64_t)t * 32 + lane) * VEC) & 31);
+                        const uint32_t z = sw[f][t] << (32 - VEC - sh);
+#pragma unroll
+                        for (int u = 0; u < VEC; ++u) {
+                            // r = +inf (nothing passed) gives 2^-inf = +0
+                            const float e = ex2(fmaf(x[t][u], kLog2e, lw - rv[f][t][u]));
+                            acc[t][u] += __uint_as_float(__float_as_uint(e) ^
+                                                         ((z << (VEC - 1 - u)) & 0x80000000u));
+                        }
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < TPW; ++t) {
+            const int64_t b = g0 + ((int64_t)t * 32 + lane) * VEC;
+#pragma unroll
+            for (int u = 0; u < VEC; ++u)
+                if (b + u < A.batch) __stcs(A.em_grads + c * A.batch + b + u, old[t][u] + acc[t][u]);
+        }
+        q0 = nq0;
+        q1 = nq1;
+        nq0 = mq0;
+        nq1 = mq1;
+        n_l = nn_l;
+        p_l = np_l;
+    }
+}
+
+template <int VEC>
+int launch_persist(const SparseBwdArgs& a, cudaStream_t s) {
+    constexpr int TPW = FL_SPBWD_PERSIST_TILES_PER_WARP, PIF = FL_SPBWD_PERSIST_PIF;
+    const int64_t groups = (a.batch + TPW * 32 * VEC - 1) / (TPW * 32 * VEC);
+    const int64_t items = a.num_elements * groups;
+    static int per_sm = 0;
+    if (per_sm == 0) {
+        FL_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &per_sm, sparse_element_grad_persist_kernel<VEC, TPW, PIF>, kWarpsPerCta * 32, 0));
+        if (per_sm < 1) per_sm = 1;
+    }
+    const int64_t grid = std::min<int64_t>((items + kWarpsPerCta - 1) / kWarpsPerCta,
+                                           (int64_t)per_sm * sm_count());
+    sparse_element_grad_persist_kernel<VEC, TPW, PIF><<<(unsigned)grid, kWarpsPerCta * 32, 0, s>>>(a, items);
+    return FL_OK;
+}
+
 template <int VEC, int J>
 int launch_cfg(const SparseBwdArgs& a, cudaStream_t s, const char* what) {
     const int64_t rows = a.num_nblocks * a.block_size;
@@ -362,17 +528,17 @@ int launch_cfg(const SparseBwdArgs& a, cudaStream_t s, const char* what) {
         sparse_param_grad_kernel<VEC, J><<<(unsigned)grid, kWarpsPerCta * 32, 0, s>>>(a);
     }
     if (a.em_grads && a.num_elements > 0) {
-        constexpr int TPW = FL_SPBWD_TILES_PER_WARP;
-        const int64_t groups = (a.batch + TPW * 32 * VEC - 1) / (TPW * 32 * VEC);
-        const int64_t grid = (a.num_elements * groups + kWarpsPerCta - 1) / kWarpsPerCta;
-        FL_REQUIRE(grid <= INT32_MAX, "%s: too many rows", what);
         if (a.fold_rows) {
             const int64_t fgrid = (rows + kWarpsPerCta - 1) / kWarpsPerCta;
             FL_REQUIRE(fgrid <= INT32_MAX, "%s: too many rows", what);
             sparse_fold_kernel<<<(unsigned)fgrid, kWarpsPerCta * 32, 0, s>>>(a);
-            sparse_element_grad_kernel<VEC, TPW, true><<<(unsigned)grid, kWarpsPerCta * 32, 0, s>>>(a);
+            if (int st = launch_persist<VEC>(a, s)) return st;
         } else {
-            sparse_element_grad_kernel<VEC, TPW, false><<<(unsigned)grid, kWarpsPerCta * 32, 0, s>>>(a);
+            constexpr int TPW = FL_SPBWD_TILES_PER_WARP;
+            const int64_t groups = (a.batch + TPW * 32 * VEC - 1) / (TPW * 32 * VEC);
+            const int64_t grid = (a.num_elements * groups + kWarpsPerCta - 1) / kWarpsPerCta;
+            FL_REQUIRE(grid <= INT32_MAX, "%s: too many rows", what);
+            sparse_element_grad_kernel<VEC, TPW><<<(unsigned)grid, kWarpsPerCta * 32, 0, s>>>(a);
         }
     }
     return FL_OK;
