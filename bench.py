@@ -337,9 +337,10 @@ class Sparse(Workload):
 class SparseFwdBwd(Workload):
     """Sparse PC sum layer forward + backward (fp32) on the default layer:
     the forward kernel, then fl_sparse_f32_bwd (parameter gradients
-    node-major; G and node_mars folded into one row per node; element
-    gradients child-major over the parent index, which is built once, outside
-    the timed region, like the workspace) with a fixed upstream gradient."""
+    G and node_mars folded into one row per node; element and parameter
+    gradients in one child-major pass over the parent index, which is built
+    once, outside the timed region, like the workspace) with a fixed upstream
+    gradient."""
     name = "sparse_fwdbwd_f32"
     dtype = "f32"
 
@@ -355,8 +356,8 @@ class SparseFwdBwd(Workload):
         self.G = torch.randn(node.shape, generator=g, device=dev)
         self.gem = torch.zeros_like(em)
         self.gw = torch.zeros_like(params)
-        self.ws = torch.empty(ext.sparse_bwd_workspace_bytes(*node.shape), dtype=torch.uint8,
-                              device=dev)
+        self.ws = torch.empty(ext.sparse_bwd_workspace_bytes(*node.shape, self.parents[1].numel()),
+                              dtype=torch.uint8, device=dev)
         self.fwd_bytes = P * batch * 4 + S * batch * 4 + S * E * (8 + 8 + 4) + S * 8
         # em read, em grads read + written, node rows and their grads read,
         # param grads read + written, the edges' cids/pids, nids, and the

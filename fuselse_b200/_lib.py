@@ -56,7 +56,7 @@ SIGNATURES = {
                           POINTER(c_int64), POINTER(c_int64), POINTER(c_int64), c_int64, _fp, _fp,
                           c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64,
                           c_void_p, c_int64, POINTER(c_int), _stream],
-    "fl_sparse_f32_bwd_workspace": [c_int64, c_int64, POINTER(c_int64)],
+    "fl_sparse_f32_bwd_workspace": [c_int64, c_int64, c_int64, POINTER(c_int64)],
     "fl_vocab_exchange_bytes": [c_int64, c_int64, POINTER(c_int64)],
     "fl_lse_vocab_exchange": [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_int, c_int,
                               _fp, _stream],

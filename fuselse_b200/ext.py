@@ -481,10 +481,13 @@ def sparse_parent_index(nids: torch.Tensor, cids: torch.Tensor, pids: torch.Tens
     return child_ptr, unit_node, unit_param
 
 
-def sparse_bwd_workspace_bytes(num_nodes: int, batch: int) -> int:
-    """Bytes of the workspace sparse_backward_float(..., fold=True) uses."""
+def sparse_bwd_workspace_bytes(num_nodes: int, batch: int, num_units: int) -> int:
+    """Bytes of the workspace sparse_backward_float(..., fold=True) uses for
+    node_mars of (num_nodes, batch) and num_units parent units (the length of
+    sparse_parent_index's unit arrays, cids.numel() * block_size)."""
     nbytes = ctypes.c_int64()
-    call("fl_sparse_f32_bwd_workspace", int(num_nodes), int(batch), ctypes.byref(nbytes))
+    call("fl_sparse_f32_bwd_workspace", int(num_nodes), int(batch), int(num_units),
+         ctypes.byref(nbytes))
     return nbytes.value
 
 
@@ -497,8 +500,9 @@ def sparse_backward_float(node_mars, node_grads, element_mars, params, nids, cid
     `parents` is sparse_parent_index(nids, cids, pids, block_size,
     element_mars.size(0)), built here if None.  fold=True (the default) first
     folds G and node_mars into one row per node so the element gradients gather
-    half the bytes; its scratch is `workspace` (a CUDA uint8 tensor of at least
-    sparse_bwd_workspace_bytes(*node_mars.shape)), allocated here if None.
+    half the bytes, and takes the parameter gradients from the same pass; its
+    scratch is `workspace` (a CUDA uint8 tensor of at least
+    sparse_bwd_workspace_bytes(*node_mars.shape, num_units)), allocated here if None.
     Returns (element_grads, param_grads)."""
     for name, t, dt in (("node_mars", node_mars, torch.float32), ("node_grads", node_grads, torch.float32),
                         ("element_mars", element_mars, torch.float32), ("params", params, torch.float32),
@@ -528,7 +532,7 @@ def sparse_backward_float(node_mars, node_grads, element_mars, params, nids, cid
     num_nblocks, num_edges = cids.shape
     ws, ws_bytes = None, 0
     if fold and element_grads is not None:
-        need = sparse_bwd_workspace_bytes(node_mars.size(0), batch)
+        need = sparse_bwd_workspace_bytes(node_mars.size(0), batch, num_units)
         if workspace is None:
             workspace = torch.empty(need, dtype=torch.uint8, device=node_mars.device)
         _check(workspace.is_cuda and workspace.dtype == torch.uint8 and workspace.is_contiguous()

@@ -290,8 +290,10 @@ int fl_sparse_log_weights(const float* params, float* logw, int64_t n,
  * skipped and set *err_flag = 1 when given.  workspace (256-byte aligned, at
  * least fl_sparse_f32_bwd_workspace bytes, contents undefined on entry and
  * exit) lets the element gradients fold each layer row's G and node_mars
- * into one gathered row first; NULL gathers both rows per parent instead
- * (same results to rounding).  The reference has no backward
+ * into one gathered row first, and, with both outputs requested, takes the
+ * parameter gradients from the same child-major pass; NULL gathers both rows
+ * per parent and the children's rows per node instead (same results to
+ * rounding).  The reference has no backward
  * (experiment_pyjuice/sparse_float_kernel.cu is forward only); no reference
  * counterpart.
  * ---------------------------------------------------------------------- */
@@ -306,8 +308,10 @@ int fl_sparse_f32_bwd(const float* node_mars, const float* node_grads,
                       void* workspace, int64_t workspace_bytes,
                       int* err_flag, fl_stream_t stream);
 
-/* Bytes of fl_sparse_f32_bwd's workspace for node_mars of (num_nodes, batch). */
-int fl_sparse_f32_bwd_workspace(int64_t num_nodes, int64_t batch, int64_t* bytes);
+/* Bytes of fl_sparse_f32_bwd's workspace for node_mars of (num_nodes, batch)
+ * and num_units parent units. */
+int fl_sparse_f32_bwd_workspace(int64_t num_nodes, int64_t batch, int64_t num_units,
+                                int64_t* bytes);
 
 #ifdef __cplusplus
 }

@@ -69,10 +69,12 @@ def test_sparse_bwd_workspace_checks_without_gpu():
     from fuselse_b200 import _lib
     L = _lib.lib()
     nbytes = ctypes.c_int64()
-    assert L.fl_sparse_f32_bwd_workspace(1000, 70, ctypes.byref(nbytes)) == _lib.FL_OK
-    # the folded rows, 256-byte aligned, then one sign word per 32 columns
-    assert nbytes.value == (1000 * 70 * 4 + 255) // 256 * 256 + 1000 * 3 * 4
-    assert L.fl_sparse_f32_bwd_workspace(-1, 70, ctypes.byref(nbytes)) == _lib.FL_ERR_INVALID_ARGUMENT
+    assert L.fl_sparse_f32_bwd_workspace(1000, 70, 5000, ctypes.byref(nbytes)) == _lib.FL_OK
+    # the folded rows, one sign word per 32 columns (each 256-byte aligned),
+    # then a partial sum per unit and 64-column group
+    r256 = lambda v: (v + 255) // 256 * 256
+    assert nbytes.value == r256(1000 * 70 * 4) + r256(1000 * 3 * 4) + 2 * 5000 * 4
+    assert L.fl_sparse_f32_bwd_workspace(-1, 70, 0, ctypes.byref(nbytes)) == _lib.FL_ERR_INVALID_ARGUMENT
     # a workspace below that size is refused before any CUDA call
     fp = lambda a: ctypes.cast(ctypes.c_void_p(a), ctypes.POINTER(ctypes.c_float))
     ip = lambda a: ctypes.cast(ctypes.c_void_p(a), ctypes.POINTER(ctypes.c_int64))

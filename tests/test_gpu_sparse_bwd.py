@@ -60,7 +60,7 @@ def test_sparse_bwd_fold_workspace(ext):
     t = to_dev(node, em, params, nids, cids, pids)
     ext.sparse_forward_float(*t, 2)
     G = torch.randn_like(t[0])
-    need = ext.sparse_bwd_workspace_bytes(*t[0].shape)
+    need = ext.sparse_bwd_workspace_bytes(*t[0].shape, t[4].numel() * 2)
     ws = torch.full((need + 4096,), 0xFF, dtype=torch.uint8, device="cuda")  # NaN-filled rows
     outs = []
     for w in (None, ws, ws):
