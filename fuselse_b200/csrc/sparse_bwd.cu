@@ -34,10 +34,14 @@
 //     order, so the result is deterministic.
 // With a workspace (the default of the Python layer):
 //   * a pre-pass folds each layer row's G and nm into one row
-//     r = (nm - log|G|) * log2(e) (+inf where the node passes nothing) and a
-//     bit mask of G's signs, so that a parent's element term is
-//     +-2^(em * log2(e) + (lw * log2(e) - r)) and its parameter term
-//     +-2^(em * log2(e) - r) (each product exact inside one fused multiply-add);
+//     r = (nm - log|G|) * log2(e) + 32 (+inf where the node passes nothing)
+//     and a bit mask of G's signs; one exponent per term,
+//     s = +-2^(em * log2(e) - r) (the product exact inside one fused
+//     multiply-add), gives the parameter term s * 2^32 (scaled once per unit)
+//     and the element term s * (w * 2^32).  The bias of 32 keeps s in range:
+//     terms below 2^-94 flush to zero (2^-126 without a workspace), and an
+//     element term would overflow only where |G| * 2^(em - nm) / 2^160 > 1,
+//     which a weight at or above the 1e-45 clamp allows only for |G| > 2^10;
 //   * the element pass runs as persistent warps that gather one row and one
 //     32-bit word per 32 columns per parent (instead of two rows), load the
 //     next children's parent indices while the current child's rows are in
@@ -107,11 +111,15 @@ struct SparseBwdArgs {
     int64_t num_nodes, num_elements, num_params, num_nblocks, batch;
     int E, block_size;
     int* err;
-    float* fold_rows;       // (num_nodes, batch): (nm - log|G|) * log2(e) of the layer's rows
+    float* fold_rows;       // (num_nodes, batch): (nm - log|G|) * log2(e) + kFoldBias of the layer's rows
     uint32_t* fold_signs;   // (num_nodes, sign_words): bit b % 32 of word b / 32 = G[n, b] < 0
     int64_t sign_words;
     float* unit_sums;       // (column groups, num_units): per-unit parameter-gradient partial sums
 };
+
+// The folded rows carry a bias of 32 in the exponent (scale 2^32): see the top of the file.
+constexpr float kFoldBias = 32.0f;
+constexpr float kFoldScale = 4294967296.0f;
 
 // Workspace of the folded path: the rows, then (each 256-byte aligned) the
 // sign words and the per-unit partial sums of the parameter gradients (one
@@ -248,7 +256,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) sparse_param_grad_kernel(Sp
     }
 }
 
-// One warp per layer row (k, p): r[n, b] = (nm - log|G|) * log2(e) (+inf
+// One warp per layer row (k, p): r[n, b] = (nm - log|G|) * log2(e) + 32 (+inf
 // where nm is -inf or G is 0) and the sign words of G, 32 columns per warp access, U
 // accesses in flight.  Rows listed twice are written twice with the same values.
 // The row's node, child and parameter indices are checked here (the passes
@@ -285,7 +293,8 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) sparse_fold_kernel(SparseBw
         for (int j = 0; j < U; ++j) {
             const int64_t b = b0 + j * 32 + lane;
             const uint32_t word = __ballot_sync(0xffffffffu, g[j] < 0.0f);
-            if (b < A.batch) out[b] = m[j] == -INFINITY ? INFINITY : (m[j] - logf(fabsf(g[j]))) * kLog2e;
+            if (b < A.batch)
+                out[b] = m[j] == -INFINITY ? INFINITY : fmaf(m[j] - logf(fabsf(g[j])), kLog2e, kFoldBias);
             if (lane == 0 && b < A.batch) signs[(b0 >> 5) + j] = word;
         }
     }
@@ -412,11 +421,8 @@ __device__ __forceinline__ void first_units(const SparseBwdArgs& A, int64_t q0, 
 // overlap the first gathers too.  The previous gradient values are read with
 // the element row, and each (c, column) is still summed by one warp in a
 // fixed order.
-// PARAMS: also the parameter gradients' per-unit partial sums over the item's
-// columns, into unit_sums[group, unit], each parameter term
-// +-2^(em * log2(e) - r) with its own exponent.  (Summing the element terms
-// instead and dividing by the weight once per unit measured 7 % faster for the
-// whole backward, but flushes the terms of tiny weights to zero.)
+// PARAMS: also the parameter gradients' per-unit partial sums (of s, scaled
+// by 2^32 afterwards) over the item's columns, into unit_sums[group, unit].
 template <int VEC, int TPW, int PIF, bool PARAMS>
 __global__ void __launch_bounds__(kWarpsPerCta * 32, FL_SPBWD_PERSIST_MIN_BLOCKS)
     sparse_element_grad_persist_kernel(SparseBwdArgs A, int64_t num_items) {
@@ -476,7 +482,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, FL_SPBWD_PERSIST_MIN_BLOCKS
                     }
                 }
             }
-            float lw_l = 0.0f;
+            float wsc_l = 0.0f;  // the clamped weight * 2^32
             for (int i = 0; i < cnt; i += PIF) {
                 float rv[PIF][TPW][VEC];
                 uint32_t sw[PIF][TPW];
@@ -495,10 +501,10 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, FL_SPBWD_PERSIST_MIN_BLOCKS
                     }
                 }
                 // the weights arrived with the first rows
-                if (i == 0) lw_l = log_weight(w_l) * kLog2e;
+                if (i == 0) wsc_l = fmaxf(w_l, 1e-45f) * kFoldScale;
 #pragma unroll
                 for (int f = 0; f < PIF; ++f) {
-                    const float lw = __shfl_sync(0xffffffffu, lw_l, (i + f) & 31);
+                    const float wsc = __shfl_sync(0xffffffffu, wsc_l, (i + f) & 31);
                     const bool live = i + f < cnt && n[f] >= 0;
                     float psum = 0.0f;
                     if (live) {
@@ -512,11 +518,9 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, FL_SPBWD_PERSIST_MIN_BLOCKS
                                 const uint32_t neg = (z << (VEC - 1 - u)) & 0x80000000u;
                                 // r = +inf (nothing passed) gives 2^-inf = +0
                                 const float e = __uint_as_float(
-                                    __float_as_uint(ex2(fmaf(x[t][u], kLog2e, lw - rv[f][t][u]))) ^ neg);
-                                acc[t][u] += e;
-                                if constexpr (PARAMS)
-                                    psum += __uint_as_float(
-                                        __float_as_uint(ex2(fmaf(x[t][u], kLog2e, -rv[f][t][u]))) ^ neg);
+                                    __float_as_uint(ex2(fmaf(x[t][u], kLog2e, -rv[f][t][u]))) ^ neg);
+                                acc[t][u] = fmaf(e, wsc, acc[t][u]);
+                                if constexpr (PARAMS) psum += e;
                             }
                         }
                     }
@@ -556,7 +560,7 @@ __global__ void __launch_bounds__(256) sparse_unit_param_kernel(SparseBwdArgs A,
     const int64_t q = __ldg(A.unit_param + u);
     if (q < 0 || q >= A.num_params) return;  // flagged by the element kernel
     const float w = __ldg(A.params + q);
-    if (w > 1e-45f) atomicAdd(A.param_grads + q, sum);
+    if (w > 1e-45f) atomicAdd(A.param_grads + q, sum * kFoldScale);
 }
 
 template <int VEC, bool PARAMS>

@@ -52,6 +52,25 @@ def test_sparse_bwd_vs_oracle(ext, E, batch, bs, fold):
     _close(gw.cpu().numpy(), want_w, f"param grads E={E} batch={batch} bs={bs}")
 
 
+@pytest.mark.parametrize("fold", [True, False], ids=["fold", "nofold"])
+def test_sparse_bwd_wide_range(ext, fold):
+    """Upstream gradients of both signs over 1e-20 .. 1e3 and weights scaled
+    down to 1e-30: the folded rows' exponent bias keeps every term in range."""
+    node, em, params, nids, cids, pids = layer(21, 500, 64, 24, 192, 1)
+    rng = np.random.default_rng(22)
+    params = (params * 10.0 ** rng.uniform(-30, 0, params.shape)).astype(np.float32)
+    t = to_dev(node, em, params, nids, cids, pids)
+    ext.sparse_forward_float(*t, 1)
+    G = (np.sign(rng.standard_normal(node.shape)) * 10.0 ** rng.uniform(-20, 3, node.shape)).astype(np.float32)
+    gem = torch.zeros_like(t[1])
+    gw = torch.zeros_like(t[2])
+    ext.sparse_backward_float(t[0], torch.from_numpy(G).cuda(), *t[1:], 1, element_grads=gem,
+                              param_grads=gw, fold=fold)
+    want_em, want_w = O.sparse_bwd_f64(t[0].cpu().numpy(), G, em, params, nids, cids, pids, 1)
+    _close(gem.cpu().numpy(), want_em, "element grads, wide range")
+    _close(gw.cpu().numpy(), want_w, "param grads, wide range")
+
+
 def test_sparse_bwd_fold_workspace(ext):
     """A caller-owned workspace (reused across calls, larger than needed)
     gives the same element gradients as one allocated per call; one that is
