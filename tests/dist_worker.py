@@ -7,7 +7,8 @@ distributed result against the single-GPU kernels on the full input:
     (rows scaled down);
   * vocab shards through the library's NVLink exchange, forward and backward;
   * batch rows: robust fp32 forward on the local rows, gathered;
-  * sparse layer over batch-column shards (fp32 and Q16.16), gathered.
+  * sparse layer over batch-column shards (fp32 and Q16.16), gathered, and its
+    backward: element gradients gathered, parameter gradients all-reduced.
 Exits non-zero on any mismatch.
 """
 import os
@@ -122,6 +123,28 @@ def main():
                  for lo, hi in (D.split_range(em.size(1), G, r) for r in range(G))]
         dist.all_gather(parts, mine)
         assert torch.equal(torch.cat(parts, dim=1), full), f"{fn.__name__}: batch-column shards differ"
+    # its backward over the same shards (data-parallel training): a column's
+    # element gradients depend on that column alone (bit-exact), the parameter
+    # gradients sum over the batch, so each rank's partial is all-reduced
+    full = node.clone()
+    ext.sparse_forward_float(full, em, params, nids, cids, pids, bs)
+    up = torch.randn(node.shape, generator=torch.Generator(device=dev).manual_seed(8), device=dev)
+    parents = ext.sparse_parent_index(nids, cids, pids, bs, em.size(0))
+    gem, gw = torch.zeros_like(em), torch.zeros_like(params)
+    ext.sparse_backward_float(full, up, em, params, nids, cids, pids, bs, element_grads=gem,
+                              param_grads=gw, parents=parents)
+    mine = full[:, c0:c1].contiguous()
+    gem_r, gw_r = torch.zeros(em.size(0), c1 - c0, device=dev), torch.zeros_like(params)
+    ext.sparse_backward_float(mine, up[:, c0:c1].contiguous(), em[:, c0:c1].contiguous(), params,
+                              nids, cids, pids, bs, element_grads=gem_r, param_grads=gw_r,
+                              parents=parents)
+    parts = [torch.empty(em.size(0), hi - lo, device=dev)
+             for lo, hi in (D.split_range(em.size(1), G, r) for r in range(G))]
+    dist.all_gather(parts, gem_r)
+    assert torch.equal(torch.cat(parts, dim=1), gem), "sparse backward: element-gradient shards differ"
+    dist.all_reduce(gw_r)
+    gerr = (gw_r - gw).abs().max().item()
+    assert gerr <= 1e-6 + 1e-5 * gw.abs().max().item(), f"sparse backward: parameter gradients err {gerr}"
     dist.barrier()
     if dist.get_rank() == 0:
         print(f"dist ok: world {G}", flush=True)
