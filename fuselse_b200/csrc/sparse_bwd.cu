@@ -91,6 +91,13 @@ constexpr int kEdgesInFlight = 4;  // children's rows gathered per step (paramet
 #ifndef FL_SPBWD_PERSIST_MIN_BLOCKS
 #define FL_SPBWD_PERSIST_MIN_BLOCKS 2
 #endif
+// Warps per CTA of the persistent pass.  4-warp CTAs at 5 per SM (20 warps,
+// a 96-register cap) spill 48-144 bytes and measured 1.57-1.65 ms for the
+// whole backward against 1.50 ms for 8-warp CTAs at 2 per SM (16 warps).
+#ifndef FL_SPBWD_PERSIST_WARPS
+#define FL_SPBWD_PERSIST_WARPS 8
+#endif
+constexpr int kPersistWarps = FL_SPBWD_PERSIST_WARPS;
 
 __device__ __forceinline__ float log_weight(float w) { return __logf(fmaxf(w, 1e-45f)); }
 
@@ -424,11 +431,11 @@ __device__ __forceinline__ void first_units(const SparseBwdArgs& A, int64_t q0, 
 // PARAMS: also the parameter gradients' per-unit partial sums (of s, scaled
 // by 2^32 afterwards) over the item's columns, into unit_sums[group, unit].
 template <int VEC, int TPW, int PIF, bool PARAMS>
-__global__ void __launch_bounds__(kWarpsPerCta * 32, FL_SPBWD_PERSIST_MIN_BLOCKS)
+__global__ void __launch_bounds__(kPersistWarps * 32, FL_SPBWD_PERSIST_MIN_BLOCKS)
     sparse_element_grad_persist_kernel(SparseBwdArgs A, int64_t num_items) {
     const int lane = threadIdx.x & 31;
-    const int64_t W = (int64_t)gridDim.x * kWarpsPerCta;
-    int64_t item = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
+    const int64_t W = (int64_t)gridDim.x * kPersistWarps;
+    int64_t item = (int64_t)blockIdx.x * kPersistWarps + (threadIdx.x >> 5);
     if (item >= num_items) return;
     const uint64_t policy = evict_last_policy();
     int64_t q0, q1, nq0, nq1, n_l, p_l;
@@ -571,13 +578,13 @@ int launch_persist_mode(const SparseBwdArgs& a, cudaStream_t s) {
     static int per_sm = 0;
     if (per_sm == 0) {
         FL_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-            &per_sm, sparse_element_grad_persist_kernel<VEC, TPW, PIF, PARAMS>, kWarpsPerCta * 32, 0));
+            &per_sm, sparse_element_grad_persist_kernel<VEC, TPW, PIF, PARAMS>, kPersistWarps * 32, 0));
         if (per_sm < 1) per_sm = 1;
     }
-    const int64_t grid = std::min<int64_t>((items + kWarpsPerCta - 1) / kWarpsPerCta,
+    const int64_t grid = std::min<int64_t>((items + kPersistWarps - 1) / kPersistWarps,
                                            (int64_t)per_sm * sm_count());
     sparse_element_grad_persist_kernel<VEC, TPW, PIF, PARAMS>
-        <<<(unsigned)grid, kWarpsPerCta * 32, 0, s>>>(a, items);
+        <<<(unsigned)grid, kPersistWarps * 32, 0, s>>>(a, items);
     if constexpr (PARAMS) {
         const int64_t ugrid = (a.num_units + 255) / 256;
         if (ugrid > INT32_MAX) return FL_ERR_INVALID_ARGUMENT;
