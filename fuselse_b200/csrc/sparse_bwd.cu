@@ -181,6 +181,22 @@ __device__ __forceinline__ void load_cols_hint(const float* row, int64_t b, int6
     }
 }
 
+// VEC streamed (evict-first) columns of a row at column b (past the batch: fill).
+template <int VEC>
+__device__ __forceinline__ void load_cols_stream(const float* row, int64_t b, int64_t batch, float fill,
+                                                 float (&v)[VEC]) {
+    if (VEC == 4 && b + 3 < batch) {
+        const float4 q = __ldcs(reinterpret_cast<const float4*>(row + b));
+        v[0] = q.x;
+        v[VEC > 1 ? 1 : 0] = q.y;
+        v[VEC > 2 ? 2 : 0] = q.z;
+        v[VEC > 3 ? 3 : 0] = q.w;
+    } else {
+#pragma unroll
+        for (int u = 0; u < VEC; ++u) v[u] = b + u < batch ? __ldcs(row + b + u) : fill;
+    }
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
@@ -450,13 +466,10 @@ __global__ void __launch_bounds__(kPersistWarps * 32, FL_SPBWD_PERSIST_MIN_BLOCK
 #pragma unroll
         for (int t = 0; t < TPW; ++t) {
             const int64_t b = g0 + ((int64_t)t * 32 + lane) * VEC;
+            load_cols_stream<VEC>(A.em + c * A.batch, b, A.batch, -INFINITY, x[t]);
+            load_cols_stream<VEC>(A.em_grads + c * A.batch, b, A.batch, 0.0f, old[t]);
 #pragma unroll
-            for (int u = 0; u < VEC; ++u) {
-                const bool in = b + u < A.batch;
-                x[t][u] = in ? __ldcs(A.em + c * A.batch + b + u) : -INFINITY;
-                old[t][u] = in ? __ldcs(A.em_grads + c * A.batch + b + u) : 0.0f;
-                acc[t][u] = 0.0f;
-            }
+            for (int u = 0; u < VEC; ++u) acc[t][u] = 0.0f;
         }
         // this item's first units (loaded during the previous item): check them
         // and start their weight loads
@@ -543,9 +556,17 @@ __global__ void __launch_bounds__(kPersistWarps * 32, FL_SPBWD_PERSIST_MIN_BLOCK
 #pragma unroll
         for (int t = 0; t < TPW; ++t) {
             const int64_t b = g0 + ((int64_t)t * 32 + lane) * VEC;
+            float* out = A.em_grads + c * A.batch + b;
+            if (VEC == 4 && b + 3 < A.batch) {
+                __stcs(reinterpret_cast<float4*>(out),
+                       make_float4(old[t][0] + acc[t][0], old[t][VEC > 1 ? 1 : 0] + acc[t][VEC > 1 ? 1 : 0],
+                                   old[t][VEC > 2 ? 2 : 0] + acc[t][VEC > 2 ? 2 : 0],
+                                   old[t][VEC > 3 ? 3 : 0] + acc[t][VEC > 3 ? 3 : 0]));
+            } else {
 #pragma unroll
-            for (int u = 0; u < VEC; ++u)
-                if (b + u < A.batch) __stcs(A.em_grads + c * A.batch + b + u, old[t][u] + acc[t][u]);
+                for (int u = 0; u < VEC; ++u)
+                    if (b + u < A.batch) __stcs(out + u, old[t][u] + acc[t][u]);
+            }
         }
         q0 = nq0;
         q1 = nq1;
