@@ -344,11 +344,9 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, FL_SPBWD_MIN_BLOCKS)
 #pragma unroll
     for (int t = 0; t < TPW; ++t) {
         const int64_t b = g0 + ((int64_t)t * 32 + lane) * VEC;
+        load_cols_stream<VEC>(A.em + c * A.batch, b, A.batch, -INFINITY, x[t]);
 #pragma unroll
-        for (int u = 0; u < VEC; ++u) {
-            x[t][u] = b + u < A.batch ? __ldcs(A.em + c * A.batch + b + u) : -INFINITY;
-            acc[t][u] = 0.0f;
-        }
+        for (int u = 0; u < VEC; ++u) acc[t][u] = 0.0f;
     }
     for (int64_t u0 = q0; u0 < q1; u0 += 32) {
         const int cnt = static_cast<int>(min((int64_t)32, q1 - u0));
