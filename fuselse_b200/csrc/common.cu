@@ -51,16 +51,16 @@ int bind_device(fl_stream_t stream, const void* ptr) {
 }
 
 int sm_count() {
-    static int cache[64] = {0};
+    static std::atomic<int> cache[64];  // per device; 0 = not yet known
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return kNumSMs;
-    if (cache[dev] == 0) {
-        int n = 0;
+    int n = cache[dev].load(std::memory_order_relaxed);
+    if (n == 0) {
         if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
             n = kNumSMs;
-        cache[dev] = n;
+        cache[dev].store(n, std::memory_order_relaxed);
     }
-    return cache[dev];
+    return n;
 }
 
 int check_launch(const char* what) {

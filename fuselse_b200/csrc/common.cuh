@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <atomic>
 #include <cstdint>
 #include <cstdio>
 #include <cstdarg>
@@ -49,6 +50,21 @@ int check_launch(const char* what);
             return FL_ERR_CUDA;                                              \
         }                                                                    \
     } while (0)
+
+// Resident CTAs per SM of `kernel` at `threads` per CTA (at least 1), cached in
+// `slot` (0 = not yet known; concurrent first calls store the same value).
+template <typename Kernel>
+cudaError_t ctas_per_sm(std::atomic<int>& slot, Kernel kernel, int threads, int& out) {
+    int v = slot.load(std::memory_order_relaxed);
+    if (v == 0) {
+        const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kernel, threads, 0);
+        if (e != cudaSuccess) return e;
+        if (v < 1) v = 1;
+        slot.store(v, std::memory_order_relaxed);
+    }
+    out = v;
+    return cudaSuccess;
+}
 
 inline bool aligned_to(const void* p, size_t a) {
     return (reinterpret_cast<uintptr_t>(p) % a) == 0;

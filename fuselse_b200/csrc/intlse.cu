@@ -261,12 +261,9 @@ int launch_cfg(const typename IK<KIND>::In* x, float* out, int64_t B, int64_t N,
     int64_t grid = B * C;
     if (C == 1 && N * (int64_t)sizeof(typename IK<KIND>::In) <= FL_INTLSE_PERSIST_ROW_BYTES) {
         // rows beyond the resident CTAs go to the same CTAs in turn
-        static int per_sm = 0;
-        if (per_sm == 0) {
-            FL_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                &per_sm, intlse_rows_kernel<KIND, LUT, CTA, D>, CTA, 0));
-            if (per_sm < 1) per_sm = 1;
-        }
+        static std::atomic<int> slot{0};
+        int per_sm = 1;
+        FL_CUDA(ctas_per_sm(slot, intlse_rows_kernel<KIND, LUT, CTA, D>, CTA, per_sm));
         grid = std::min<int64_t>(grid, (int64_t)per_sm * sm_count());
     }
     cudaLaunchConfig_t cfg = {};

@@ -602,12 +602,10 @@ int launch_persist_mode(const SparseBwdArgs& a, cudaStream_t s) {
     constexpr int TPW = FL_SPBWD_PERSIST_TILES_PER_WARP, PIF = FL_SPBWD_PERSIST_PIF;
     const int64_t groups = (a.batch + TPW * 32 * VEC - 1) / (TPW * 32 * VEC);
     const int64_t items = a.num_elements * groups;
-    static int per_sm = 0;
-    if (per_sm == 0) {
-        FL_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-            &per_sm, sparse_element_grad_persist_kernel<VEC, TPW, PIF, PARAMS>, kPersistWarps * 32, 0));
-        if (per_sm < 1) per_sm = 1;
-    }
+    static std::atomic<int> slot{0};
+    int per_sm = 1;
+    FL_CUDA(ctas_per_sm(slot, sparse_element_grad_persist_kernel<VEC, TPW, PIF, PARAMS>,
+                        kPersistWarps * 32, per_sm));
     const int64_t grid = std::min<int64_t>((items + kPersistWarps - 1) / kPersistWarps,
                                            (int64_t)per_sm * sm_count());
     sparse_element_grad_persist_kernel<VEC, TPW, PIF, PARAMS>
