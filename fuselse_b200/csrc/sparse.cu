@@ -19,7 +19,8 @@
 //     stored evict-first, so the slice, not the output stream, holds the L2;
 //   * each thread owns one node x 4 adjacent columns (16-byte gathers), 8
 //     gathers in flight, full groups of 8 edges without predicates;
-//   * fp32: online (max, sum-exp) with one EX2 per logit; Q16.16: the
+//   * fp32: online (max, sum-exp) in the log2 domain, one FMA and one EX2 per
+//     logit (log-weights staged times log2(e)); Q16.16: the
 //     reference's per-edge chain order (edge e feeds chain e mod ET, chains
 //     merged by the ET-lane butterfly) evaluated inside one thread.
 #include "common.cuh"
@@ -93,7 +94,8 @@ struct Acc<false, VEC, ET> {
 #pragma unroll
         for (int c = 0; c < VEC; ++c) { m[c] = -INFINITY; s[c] = 0.0f; }
     }
-    // logits[g][c] for kGroup edges starting at edge e0 (unused ones -inf)
+    // logits[g][c] times log2(e) for kGroup edges starting at edge e0 (unused
+    // ones -inf); the state's max m is in the same log2 units
     __device__ __forceinline__ void fold(const float (&lg)[kGroup][VEC], int /*e0*/, int nvalid,
                                          LaneLut) {
 #pragma unroll
@@ -103,16 +105,19 @@ struct Acc<false, VEC, ET> {
             for (int g = 1; g < kGroup; ++g) mx = max_nan(mx, lg[g][c]);
             const float M = max_nan(m[c], mx);
             const float Ms = safe_max(M);
-            float a = s[c] * exp_from(m[c], Ms);
+            float a = s[c] * ex2(m[c] - Ms);
 #pragma unroll
             for (int g = 0; g < kGroup; ++g)
-                if (g < nvalid) a += exp_from(lg[g][c], Ms);
+                if (g < nvalid) a += ex2(lg[g][c] - Ms);
             s[c] = a;
             m[c] = M;
         }
     }
     __device__ __forceinline__ float result(int c, LaneLut) const {
-        return ms_finalize(m[c], s[c], -1.0e30f);
+        const float m2 = m[c];
+        if (m2 != m2 || m2 == INFINITY) return m2;  // NaN anywhere, else +inf
+        if (m2 == -INFINITY) return -1.0e30f;       // no finite logit
+        return fmaf(m2, kLn2, logf(s[c]));
     }
 };
 
@@ -198,7 +203,10 @@ __global__ void __launch_bounds__(kThreads) sparse_kernel(SparseArgs A) {
         const int64_t pid = A.pids[nb * E + e] + p;
         const bool ok = cid >= 0 && cid < A.num_elements && pid >= 0 && pid < A.num_params;
         s_cid[i] = ok ? static_cast<int>(cid) : -1;
-        s_lw[i] = ok ? log_weight(__ldg(A.params + pid)) : 0.0f;
+        // fp32 stages lw * log2(e) (its logits are formed as x * log2(e) + that);
+        // Q16.16 keeps lw, the reference's conversion input being x + lw
+        s_lw[i] = ok ? (Q16 ? log_weight(__ldg(A.params + pid))
+                            : log_weight(__ldg(A.params + pid)) * kLog2e) : 0.0f;
     }
     for (int ln = threadIdx.x; ln < nn; ln += kThreads) {
         const int64_t k = n0 + ln;
@@ -255,7 +263,7 @@ __global__ void __launch_bounds__(kThreads) sparse_kernel(SparseArgs A) {
                 for (int g = 0; g < kGroup; ++g) {
                     const float w = g < nvalid ? wp[e0 + g] : 0.0f;
 #pragma unroll
-                    for (int c = 0; c < VEC; ++c) lg[g][c] += w;
+                    for (int c = 0; c < VEC; ++c) lg[g][c] = Q16 ? lg[g][c] + w : fmaf(lg[g][c], kLog2e, w);
                 }
                 acc.fold(lg, e0, nvalid, lut);
             };
