@@ -78,10 +78,12 @@ constexpr int kEdgesInFlight = 4;  // children's rows gathered per step (paramet
 #define FL_SPBWD_MIN_BLOCKS 3
 #endif
 // The folded path (persistent, index-prefetching warps).  Measured on B200
-// for the same layer, element gradients alone: tiles 2 with 1 / 2 / 3 / 4
-// parents in flight at 2 CTAs per SM -> 1.56 / 1.41 / 1.34 / 1.64 ms; tiles 1
-// -> 1.68-1.99 ms; tiles 4 -> 1.80-2.02 ms; the non-persistent kernel on the
-// folded rows 1.69-2.13 ms and on G and nm 1.68 ms.
+// for the same layer while it computed the element gradients alone: tiles 2
+// with 1 / 2 / 3 / 4 parents in flight at 2 CTAs per SM -> 1.56 / 1.41 / 1.34
+// / 1.64 ms; tiles 1 -> 1.68-1.99 ms; tiles 4 -> 1.80-2.02 ms; the
+// non-persistent kernel on the folded rows 1.69-2.13 ms and on G and nm
+// 1.68 ms.  With the parameter terms in the same pass (whole backward): 1 / 2
+// / 4 parents in flight 1.58-1.68 ms against 1.50 ms for 3.
 #ifndef FL_SPBWD_PERSIST_TILES_PER_WARP
 #define FL_SPBWD_PERSIST_TILES_PER_WARP 2
 #endif
