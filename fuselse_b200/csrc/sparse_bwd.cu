@@ -610,6 +610,10 @@ int launch_persist_mode(const SparseBwdArgs& a, cudaStream_t s) {
                         kPersistWarps * 32, per_sm));
     const int64_t grid = std::min<int64_t>((items + kPersistWarps - 1) / kPersistWarps,
                                            (int64_t)per_sm * sm_count());
+    // units outside every child's range (edges whose child index is out of
+    // range sit at the index's tail) are never visited: their sums stay 0
+    if constexpr (PARAMS)
+        FL_CUDA(cudaMemsetAsync(a.unit_sums, 0, (size_t)(groups * a.num_units) * sizeof(float), s));
     sparse_element_grad_persist_kernel<VEC, TPW, PIF, PARAMS>
         <<<(unsigned)grid, kPersistWarps * 32, 0, s>>>(a, items);
     if constexpr (PARAMS) {

@@ -124,6 +124,34 @@ def test_sparse_bwd_bad_indices_set_flag(ext):
         assert torch.isfinite(gem).all() and torch.isfinite(gw).all()
 
 
+def test_sparse_bwd_index_built_from_bad_child(ext):
+    """An edge whose child is out of range, in the parent index too: the index
+    leaves it out of every child's range; both paths skip it, flag it and agree,
+    whatever the workspace held before."""
+    node, em, params, nids, cids, pids = layer(31, 100, 12, 8, 64, 1)
+    t = to_dev(node, em, params, nids, cids, pids)
+    ext.sparse_forward_float(*t, 1)
+    cids_bad = t[4].clone()
+    cids_bad[2, 5] = 100  # == num_elements
+    parents = ext.sparse_parent_index(t[3], cids_bad, t[5], 1, 100)
+    G = torch.randn_like(t[0])
+    outs = []
+    for fold in (True, False):
+        err = torch.zeros(1, dtype=torch.int32, device="cuda")
+        ws = None
+        if fold:  # 0x7f bytes: every float slot reads 3.4e38 unless written
+            ws = torch.full((ext.sparse_bwd_workspace_bytes(*t[0].shape, parents[1].numel()),), 0x7F,
+                            dtype=torch.uint8, device="cuda")
+        gem, gw = torch.zeros_like(t[1]), torch.zeros_like(t[2])
+        ext.sparse_backward_float(t[0], G, t[1], t[2], t[3], cids_bad, t[5], 1, element_grads=gem,
+                                  param_grads=gw, parents=parents, err_flag=err, fold=fold, workspace=ws)
+        assert int(err.item()) == 1
+        assert torch.isfinite(gem).all() and torch.isfinite(gw).all()
+        outs.append((gem, gw))
+    for a, b in zip(*outs):
+        torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-6 * max(b.abs().max().item(), 1e-30))
+
+
 def _torch_layer(node_mars, em, params, nids, cids, pids, bs):
     """The reference experiment's torch restatement (run_pyjuice.py:90-119),
     with the kernels' 1e-45 floor, as a differentiable function."""
