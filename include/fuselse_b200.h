@@ -289,7 +289,7 @@ int fl_sparse_log_weights(const float* params, float* logw, int64_t n,
  * num_units is the length of those two arrays.  Indices out of range are
  * skipped and set *err_flag = 1 when given.  workspace (256-byte aligned, at
  * least fl_sparse_f32_bwd_workspace bytes, contents undefined on entry and
- * exit) lets the element gradients fold each layer row's G and node_mars
+ * exit, one call in flight per workspace) lets the element gradients fold each layer row's G and node_mars
  * into one gathered row first, and, with both outputs requested, takes the
  * parameter gradients from the same child-major pass; NULL gathers both rows
  * per parent and the children's rows per node instead (same results to
