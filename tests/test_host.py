@@ -154,30 +154,47 @@ def test_row_layout_cases():
 
 
 # ---------------------------------------------------------------- sparse backward oracle
-def test_sparse_bwd_oracle_matches_torch_autograd_cpu():
+@pytest.mark.parametrize("tied", [False, True], ids=["untied", "tied"])
+def test_sparse_bwd_oracle_matches_torch_autograd_cpu(tied):
     """The fp64 gradient oracle against torch autograd of the layer formula
     (run_pyjuice.py:90-119 with the 1e-45 floor), block_size 2, shared
-    children and one weight below the floor."""
+    children and one weight below the floor; tied: several edges share a
+    parameter, and one node's children are all -inf.  Such a node's
+    node_mars is -inf and it passes no gradient (torch's logsumexp backward
+    gives NaN there, which tied parameters would spread), so torch's graph is
+    built over the live nodes only and compared with the oracle on the full
+    layer."""
     rng = np.random.default_rng(0)
     P, K, E, batch, bs = 40, 6, 5, 7, 2
     em = rng.standard_normal((P, batch)) * 3 - 5
     nm0 = np.zeros((K * bs + 3, batch))
     nids = np.arange(K) * bs + 3
-    cids = rng.integers(0, P, size=(K, E))
+    cids = rng.integers(0, P - 1, size=(K, E))
     pids = np.arange(K * E).reshape(K, E) * bs
     params = rng.random(K * E * bs) + 0.05
     params[4] = 1e-50
+    live = np.ones(K, bool)
+    if tied:
+        pids = pids % (3 * E * bs)   # nodes 3-5 reuse nodes 0-2's parameters
+        cids[1] = P - 1              # node 1's children: all the -inf row
+        em[P - 1] = -np.inf
+        live[1] = False
     G = rng.standard_normal(nm0.shape)
 
     em_t = torch.tensor(em, requires_grad=True)
     w_t = torch.tensor(params, requires_grad=True)
-    n = torch.tensor((nids[:, None] + np.arange(bs)[None, :]).reshape(-1))
-    c = torch.tensor(np.repeat(cids[:, None, :], bs, axis=1).reshape(K * bs, E))
-    q = torch.tensor((pids[:, None, :] + np.arange(bs)[None, :, None]).reshape(K * bs, E))
+    ar = np.arange(bs)
+    n = (nids[:, None] + ar[None, :])                                   # (K, bs)
+    c = np.repeat(cids[:, None, :], bs, axis=1)                         # (K, bs, E)
+    q = pids[:, None, :] + ar[None, :, None]                            # (K, bs, E)
     out = torch.tensor(nm0).clone()
-    out[n] = torch.logsumexp(em_t[c] + w_t[q].clamp(min=1e-45).log().unsqueeze(-1), dim=1)
+    nl, cl, ql = (torch.tensor(a[live].reshape(-1, *a.shape[2:])) for a in (n, c, q))
+    out[nl] = torch.logsumexp(em_t[cl] + w_t[ql].clamp(min=1e-45).log().unsqueeze(-1), dim=1)
+    nm = out.detach().numpy().copy()
+    nm[n[~live].reshape(-1)] = -np.inf                                  # the dead node's forward value
     (out * torch.tensor(G)).sum().backward()
-    gem, gw = O.sparse_bwd_f64(out.detach().numpy(), G, em, params, nids, cids, pids, bs)
+    gem, gw = O.sparse_bwd_f64(nm, G, em, params, nids, cids, pids, bs)
     np.testing.assert_allclose(gem, em_t.grad.numpy(), rtol=1e-10, atol=1e-12)
     np.testing.assert_allclose(gw, w_t.grad.numpy(), rtol=1e-10, atol=1e-12)
     assert gw[4] == 0.0
+    assert np.isfinite(gem).all() and np.isfinite(gw).all()
