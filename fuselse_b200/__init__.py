@@ -13,6 +13,10 @@ libfuselse_b200.so (include/fuselse_b200.h).  `fuselse_b200.distributed`
 shards rows across GPUs and combines vocab-sharded rows over NCCL or the
 library's own NVLink exchange.  `selective_log_softmax(logits, index)` is the
 fused per-token log-probability (target gather + LSE in one pass).
+`fuselse_b200.pc` has the pyjuice `SumLayer._forward_sparse` hook and a
+differentiable sparse sum layer (its backward on the device too), and
+`fuselse_b200.host` runs the forward and backward on rows held in pinned host
+memory with the copies overlapped.
 """
 from . import ext
 from .autograd import make_fuselse_logsumexp
