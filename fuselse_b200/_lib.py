@@ -61,6 +61,12 @@ SIGNATURES = {
     "fl_lse_vocab_exchange": [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_int, c_int,
                               _fp, _stream],
     "fl_lse_vocab_exchange_noalloc": [c_void_p, c_int, c_int64, c_int64, _fp, _stream],
+    "fl_vocab_exchange_set_wait_limit": [c_int64, POINTER(c_int64)],
+    "fl_ipc_buffer_alloc": [c_int, c_int64, POINTER(c_void_p), c_void_p],
+    "fl_ipc_buffer_open": [c_int, c_void_p, POINTER(c_void_p)],
+    "fl_ipc_buffer_close": [c_int, c_void_p],
+    "fl_ipc_buffer_free": [c_int, c_void_p],
+    "fl_binary_version": [c_int, POINTER(c_int)],
 }
 
 

@@ -72,7 +72,22 @@ int check_launch(const char* what) {
     return FL_OK;
 }
 
+// A kernel of this library, for querying the binary the loaded module holds.
+__global__ void probe_kernel(int* p) {
+    if (p) *p = 0;
+}
+
 }  // namespace fl
+
+extern "C" int fl_binary_version(int device, int* version) {
+    fl::clear_error();
+    FL_REQUIRE(device >= 0 && version, "fl_binary_version: bad arguments");
+    FL_CUDA(cudaSetDevice(device));
+    cudaFuncAttributes attr;
+    FL_CUDA(cudaFuncGetAttributes(&attr, fl::probe_kernel));
+    *version = attr.binaryVersion;
+    return FL_OK;
+}
 
 extern "C" const char* fl_last_error(void) { return fl::g_last_error.c_str(); }
 

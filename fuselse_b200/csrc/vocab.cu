@@ -13,7 +13,8 @@
 //     this rank delivered; the store is idempotent (every CTA stores the same
 //     epoch), so no CTA depends on another having been scheduled.  Then every
 //     CTA waits until every rank's flag shows this call (acquire, system
-//     scope; bounded by an iteration cap and a 2 s clock limit, after which it
+//     scope; bounded by an iteration cap and a clock limit, 2 s unless set by
+//     fl_vocab_exchange_set_wait_limit, after which it
 //     writes NaN rows and sets a sticky error word), merges the G pairs of
 //     each row and finishes lse = M + log(sum_g s_g exp(m_g - M)); the last
 //     CTA to finish advances the call epoch.  With G == 1 there is nothing to
@@ -34,6 +35,7 @@
 #include "rows.cuh"
 
 #include <cuda_fp16.h>
+#include <cstring>
 
 namespace fl {
 namespace {
@@ -43,12 +45,6 @@ constexpr int64_t kHeaderBytes = 256;
 
 __host__ __device__ inline int64_t flags_bytes(int64_t G) { return (G * 4 + 255) / 256 * 256; }
 __host__ __device__ inline int64_t pairs_offset(int64_t G) { return kHeaderBytes + flags_bytes(G); }
-
-__device__ __forceinline__ uint64_t global_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     uint32_t v;
@@ -86,15 +82,18 @@ __global__ void __launch_bounds__(kRowsPerCta * 32) vocab_scatter_kernel(
 }
 
 constexpr int kCombineThreads = 256;
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr int64_t kDefaultWaitNs = 2000000000LL;  // 2 s
 constexpr uint32_t kWaitLimitIters = 1u << 26;
+
+// Limit of one combine CTA's wait for one peer's flag, read at each launch.
+std::atomic<int64_t> g_wait_limit_ns{kDefaultWaitNs};
 
 // One thread per row; every CTA publishes this rank's delivery, then waits
 // for the flags itself.  The last CTA to finish advances the finished-call
 // epoch.
 __global__ void __launch_bounds__(kCombineThreads) vocab_combine_kernel(
     unsigned char* const* __restrict__ peers, unsigned char* __restrict__ local,
-    float* __restrict__ out, int64_t B, int rank, int G) {
+    float* __restrict__ out, int64_t B, int rank, int G, uint64_t wait_ns) {
     __shared__ int timed_out;
     uint32_t* header = reinterpret_cast<uint32_t*>(local);
     const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(header + 2);
@@ -111,7 +110,7 @@ __global__ void __launch_bounds__(kCombineThreads) vocab_combine_kernel(
         const uint64_t t0 = global_ns();
         for (uint32_t it = 0;; ++it) {
             if ((int32_t)(ld_acquire_sys(flag) - epoch) >= 0) break;
-            if (it >= kWaitLimitIters || global_ns() - t0 > kWaitLimitNs) {
+            if (it >= kWaitLimitIters || global_ns() - t0 > wait_ns) {
                 atomicExch(&timed_out, 1);
                 break;
             }
@@ -153,7 +152,8 @@ using namespace fl;
 
 extern "C" int fl_vocab_exchange_bytes(int64_t G, int64_t B, int64_t* bytes) {
     clear_error();
-    FL_REQUIRE(G >= 1 && G <= 1024 && B >= 0 && bytes, "fl_vocab_exchange_bytes: bad arguments");
+    FL_REQUIRE(G >= 1 && G <= 1024 && B >= 0 && B <= (1LL << 40) && bytes,
+               "fl_vocab_exchange_bytes: bad arguments");
     *bytes = pairs_offset(G) + 2 * G * B * (int64_t)sizeof(float2);
     return FL_OK;
 }
@@ -185,8 +185,77 @@ extern "C" int fl_lse_vocab_exchange(const void* x, int dtype, int64_t B, int64_
             reinterpret_cast<const __half*>(x), B, N, peers, local, rank, G);
     if (int st = check_launch(what)) return st;
     const int64_t cgrid = (B + kCombineThreads - 1) / kCombineThreads;
-    vocab_combine_kernel<<<(unsigned)cgrid, kCombineThreads, 0, s>>>(peers, local, out, B, rank, G);
+    const uint64_t wait_ns = static_cast<uint64_t>(g_wait_limit_ns.load(std::memory_order_relaxed));
+    vocab_combine_kernel<<<(unsigned)cgrid, kCombineThreads, 0, s>>>(peers, local, out, B, rank, G,
+                                                                     wait_ns);
     return check_launch(what);
+}
+
+extern "C" int fl_vocab_exchange_set_wait_limit(int64_t ns, int64_t* previous) {
+    clear_error();
+    FL_REQUIRE(ns >= 1000000 && ns <= 60000000000LL,
+               "fl_vocab_exchange_set_wait_limit: %lld ns outside [1 ms, 60 s]", (long long)ns);
+    const int64_t old = g_wait_limit_ns.exchange(ns, std::memory_order_relaxed);
+    if (previous) *previous = old;
+    return FL_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Exchange buffers shared across processes by CUDA IPC.  An IPC handle names a
+// whole cudaMalloc allocation, so the buffer is allocated here rather than by
+// the caller's pool; the importing process maps it with plain peer mappings
+// (cudaIpcOpenMemHandle): unicast peer mappings only, no NVLS group.
+// ---------------------------------------------------------------------------
+static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+
+extern "C" int fl_ipc_buffer_alloc(int device, int64_t bytes, void** buf, void* ipc_handle) {
+    clear_error();
+    const char* what = "fl_ipc_buffer_alloc";
+    FL_REQUIRE(device >= 0 && bytes > 0 && bytes <= (1LL << 40) && buf && ipc_handle,
+               "%s: bad arguments", what);
+    FL_CUDA(cudaSetDevice(device));
+    void* p = nullptr;
+    FL_CUDA(cudaMalloc(&p, static_cast<size_t>(bytes)));
+    cudaError_t e = cudaMemset(p, 0, static_cast<size_t>(bytes));
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        set_error("%s: %s", what, cudaGetErrorString(e));
+        return FL_ERR_CUDA;
+    }
+    memcpy(ipc_handle, &h, sizeof(h));
+    *buf = p;
+    return FL_OK;
+}
+
+extern "C" int fl_ipc_buffer_open(int device, const void* ipc_handle, void** buf) {
+    clear_error();
+    FL_REQUIRE(device >= 0 && ipc_handle && buf, "fl_ipc_buffer_open: bad arguments");
+    FL_CUDA(cudaSetDevice(device));
+    cudaIpcMemHandle_t h;
+    memcpy(&h, ipc_handle, sizeof(h));
+    FL_CUDA(cudaIpcOpenMemHandle(buf, h, cudaIpcMemLazyEnablePeerAccess));
+    return FL_OK;
+}
+
+extern "C" int fl_ipc_buffer_close(int device, void* buf) {
+    clear_error();
+    FL_REQUIRE(device >= 0 && buf, "fl_ipc_buffer_close: bad arguments");
+    FL_CUDA(cudaSetDevice(device));
+    FL_CUDA(cudaIpcCloseMemHandle(buf));
+    return FL_OK;
+}
+
+extern "C" int fl_ipc_buffer_free(int device, void* buf) {
+    clear_error();
+    FL_REQUIRE(device >= 0, "fl_ipc_buffer_free: bad device");
+    if (!buf) return FL_OK;
+    FL_CUDA(cudaSetDevice(device));
+    FL_CUDA(cudaDeviceSynchronize());  // no kernel of this process still uses it
+    FL_CUDA(cudaFree(buf));
+    return FL_OK;
 }
 
 // ---------------------------------------------------------------------------
@@ -243,9 +312,10 @@ extern "C" int fl_lse_vocab_exchange_noalloc(const void* x, int dtype, int64_t B
     const char* what = "fl_lse_vocab_exchange_noalloc";
     FL_REQUIRE(dtype == 0 || dtype == 1, "%s: dtype must be 0 (fp32) or 1 (fp16)", what);
     FL_REQUIRE(B >= 0 && N >= 0, "%s: negative shape", what);
-    const int64_t need = pairs_offset(1) + 2 * B * (int64_t)sizeof(float2);
+    // the row count is compared before any arithmetic on it (a byte count
+    // formed from a huge B would wrap around and pass)
     const int64_t max_rows = (kNoAllocBytes - pairs_offset(1)) / (2 * (int64_t)sizeof(float2));
-    FL_REQUIRE(need <= kNoAllocBytes,
+    FL_REQUIRE(B <= max_rows,
                "%s: B=%lld rows exceed the static exchange buffer (%lld bytes, at most %lld rows)",
                what, (long long)B, (long long)kNoAllocBytes, (long long)max_rows);
     FL_REQUIRE(B == 0 || out, "%s: out is NULL", what);
@@ -268,6 +338,7 @@ extern "C" int fl_lse_vocab_exchange_noalloc(const void* x, int dtype, int64_t B
             reinterpret_cast<const __half*>(x), B, N, d.peers, d.exchange, 0, 1);
     if (int st = check_launch(what)) return st;
     const int64_t cgrid = (B + kCombineThreads - 1) / kCombineThreads;
-    vocab_combine_kernel<<<(unsigned)cgrid, kCombineThreads, 0, s>>>(d.peers, d.exchange, out, B, 0, 1);
+    vocab_combine_kernel<<<(unsigned)cgrid, kCombineThreads, 0, s>>>(d.peers, d.exchange, out, B, 0, 1,
+                                                                     0);  // G = 1: no wait
     return check_launch(what);
 }

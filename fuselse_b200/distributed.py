@@ -120,6 +120,15 @@ def vocab_sharded_logsumexp_grad(x_shard: torch.Tensor, exchange: Callable,
     return VocabShardedLogSumExp.apply(x_shard, exchange, backward_fn)
 
 
+class _RawDeviceBytes:
+    """A raw device allocation exposed to torch (no ownership) through the CUDA
+    array interface, so torch ops can zero it or read its header words."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1",
+                                         "data": (ptr, False), "version": 3, "strides": None}
+
+
 class VocabShardExchange:
     """Vocab-sharded log-sum-exp with the (max, sumexp) exchange done by this
     library's own kernels over NVLink peer memory (fl_lse_vocab_exchange): the
@@ -128,15 +137,17 @@ class VocabShardExchange:
     release of the call's epoch, waits (bounded) for all ranks and finishes
     the rows.  No NCCL call on the data path.
 
-    The exchange buffer is a torch symmetric-memory allocation (peer mappings
-    of every rank's buffer on every device), made once per (group, rows).
-    Every rank must call with the same B, in the same sequence.
+    Each rank's exchange buffer is its own cudaMalloc allocation
+    (fl_ipc_buffer_alloc), shared with the other ranks by CUDA IPC handles
+    (exchanged once over the process group) and mapped there with plain peer
+    mappings (fl_ipc_buffer_open): unicast peer mappings only, no NVLS group.
+    Made once per (group, rows); close() (or garbage collection) unmaps the
+    peers' buffers and frees this rank's after a barrier.  Every rank must
+    call with the same B, in the same sequence.
     """
 
     def __init__(self, rows: int, group=None, device=None):
         import ctypes
-
-        import torch.distributed._symmetric_memory as symm
 
         from . import _lib
         self.group = group if group is not None else dist.group.WORLD
@@ -145,18 +156,31 @@ class VocabShardExchange:
         self.rows = rows
         self.device = torch.device(device) if device is not None else torch.device(
             "cuda", torch.cuda.current_device())
+        dev = self.device.index
         nbytes = ctypes.c_int64()
         _lib.call("fl_vocab_exchange_bytes", self.G, rows, ctypes.byref(nbytes))
-        self.buf = symm.empty(nbytes.value, dtype=torch.uint8, device=self.device)
-        self.buf.zero_()
-        torch.cuda.synchronize(self.device)
-        try:
-            self.handle = symm.rendezvous(self.buf, self.group)
-        except RuntimeError:
-            symm.enable_symm_mem_for_group(self.group.group_name)
-            self.handle = symm.rendezvous(self.buf, self.group)
-        self.peer_array = self.handle.buffer_ptrs_dev
-        dist.barrier(self.group)  # every rank's buffer is zeroed before anyone writes
+        self.nbytes = nbytes.value
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * 64)()
+        _lib.call("fl_ipc_buffer_alloc", dev, self.nbytes, ctypes.byref(ptr), handle)
+        self._own = ptr.value
+        self._opened = []
+        handles = [None] * self.G
+        dist.all_gather_object(handles, bytes(handle), group=self.group)
+        addrs = []
+        for q, h in enumerate(handles):
+            if q == self.rank:
+                addrs.append(self._own)
+                continue
+            peer = ctypes.c_void_p()
+            _lib.call("fl_ipc_buffer_open", dev, (ctypes.c_ubyte * 64).from_buffer_copy(h),
+                      ctypes.byref(peer))
+            self._opened.append(peer.value)
+            addrs.append(peer.value)
+        self.buf = torch.as_tensor(_RawDeviceBytes(self._own, self.nbytes), device=self.device)
+        self._ptrs = torch.tensor(addrs, dtype=torch.int64, device=self.device)
+        self.peer_array = self._ptrs.data_ptr()
+        dist.barrier(self.group)  # every rank's buffer is mapped before anyone writes
 
     @classmethod
     def single_rank(cls, rows: int, device="cuda"):
@@ -166,15 +190,41 @@ class VocabShardExchange:
         from . import _lib
         self = cls.__new__(cls)
         self.group, self.G, self.rank, self.rows = None, 1, 0, rows
+        self._own, self._opened = None, []
         self.device = torch.device(device)
         if self.device.index is None:
             self.device = torch.device("cuda", torch.cuda.current_device())
         nbytes = ctypes.c_int64()
         _lib.call("fl_vocab_exchange_bytes", 1, rows, ctypes.byref(nbytes))
+        self.nbytes = nbytes.value
         self.buf = torch.zeros(nbytes.value, dtype=torch.uint8, device=self.device)
         self._ptrs = torch.tensor([self.buf.data_ptr()], dtype=torch.int64, device=self.device)
         self.peer_array = self._ptrs.data_ptr()
         return self
+
+    def close(self, barrier: bool = True) -> None:
+        """Unmaps the peers' buffers and frees this rank's.  With barrier=True
+        (every rank calls close) no rank frees its buffer while another still
+        has it mapped."""
+        from . import _lib
+        if not getattr(self, "_own", None):
+            return
+        torch.cuda.synchronize(self.device)
+        dev = self.device.index
+        for p in self._opened:
+            _lib.call("fl_ipc_buffer_close", dev, p)
+        self._opened = []
+        if barrier and self.group is not None:
+            dist.barrier(self.group)
+        self.buf = None
+        _lib.call("fl_ipc_buffer_free", dev, self._own)
+        self._own = None
+
+    def __del__(self):
+        try:
+            self.close(barrier=False)
+        except Exception:
+            pass
 
     def __call__(self, x_shard: torch.Tensor) -> torch.Tensor:
         import ctypes

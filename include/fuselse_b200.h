@@ -3,9 +3,11 @@
  *
  * Every entry point takes plain device pointers, int64 sizes and a CUDA
  * stream, launches its kernels asynchronously on that stream and returns a
- * status code (FL_OK == 0).  Nothing here allocates device memory: outputs
- * are caller-owned buffers.  On a non-zero status, fl_last_error() returns a
- * message for the calling thread.
+ * status code (FL_OK == 0).  No compute entry point allocates device
+ * memory: outputs are caller-owned buffers (the fl_ipc_buffer_* helpers,
+ * which create and map buffers shared between processes, are the
+ * exception).  On a non-zero status, fl_last_error() returns a message for
+ * the calling thread.
  *
  * Pointer rules shared by all entry points:
  *   - all pointers are device (or managed) memory of the device that owns
@@ -40,6 +42,10 @@ const char* fl_last_error(void);
 
 /* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
 int fl_version(void);
+
+/* The binary version (major*10 + minor, 100 for sm_100a) of the kernels this
+ * library loads on `device`, from cudaFuncGetAttributes (needs a GPU). */
+int fl_binary_version(int device, int* version);
 
 /* ------------------------------------------------------------------------
  * FuseLSE fp32 forward: out[b] = log(sum_n exp(x[b, n])), x (B, N) fp32.
@@ -173,16 +179,45 @@ int fl_lse_combine(const float* ms, float* out, int64_t G, int64_t B,
  * fl_vocab_exchange_bytes(G, B) bytes (256-byte aligned, zero-filled once
  * before first use on every rank, then left to the library), and
  * `peer_bufs` a DEVICE array of the G ranks' buffer addresses as mapped on
- * this device (a symmetric allocation; peer_bufs[rank] == local_buf).
+ * this device (e.g. buffers of fl_ipc_buffer_alloc mapped with
+ * fl_ipc_buffer_open; peer_bufs[rank] == local_buf).
  * Writes out (B,) fp32 on every rank.  Every rank must make the same
  * sequence of calls with the same B.  If a peer's contribution does not
- * arrive within 2 s the rows are NaN and the 32-bit word at byte offset 4
- * of local_buf becomes non-zero (sticky).
+ * arrive within the wait limit (2 s unless changed by
+ * fl_vocab_exchange_set_wait_limit) the rows are NaN and the 32-bit word at
+ * byte offset 4 of local_buf becomes non-zero (sticky); the call epoch
+ * still advances, so the buffer must be zero-filled again on every rank
+ * before the group makes another exchange.
  * ---------------------------------------------------------------------- */
 int fl_vocab_exchange_bytes(int64_t G, int64_t B, int64_t* bytes);
 int fl_lse_vocab_exchange(const void* x, int dtype, int64_t B, int64_t N,
                           void* const* peer_bufs, void* local_buf, int rank, int G,
                           float* out, fl_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Exchange buffers shared between processes by CUDA IPC (no reference
+ * counterpart).  These four are the only entry points that allocate or map
+ * device memory: a CUDA IPC handle names a whole cudaMalloc allocation, so a
+ * buffer meant for other processes cannot come from a caller's pool.
+ *   fl_ipc_buffer_alloc: `bytes` zero-filled bytes on `device`, 256-byte
+ *     aligned; *buf = its address here, ipc_handle (64 bytes) = its handle
+ *     for the other processes;
+ *   fl_ipc_buffer_open: maps another process's buffer on `device` (plain
+ *     unicast peer mapping, no NVLS group) and returns its address here;
+ *   fl_ipc_buffer_close: unmaps a buffer opened by fl_ipc_buffer_open;
+ *   fl_ipc_buffer_free: waits for the device and frees a buffer of
+ *     fl_ipc_buffer_alloc (every other process must have closed it first).
+ * ---------------------------------------------------------------------- */
+int fl_ipc_buffer_alloc(int device, int64_t bytes, void** buf, void* ipc_handle);
+int fl_ipc_buffer_open(int device, const void* ipc_handle, void** buf);
+int fl_ipc_buffer_close(int device, void* buf);
+int fl_ipc_buffer_free(int device, void* buf);
+
+/* Sets the limit of the exchange's wait for a peer (per combine CTA and
+ * peer), in nanoseconds within [1e6, 6e10], for launches made after the
+ * call, process-wide; *previous (if not NULL) receives the old limit.
+ * No reference counterpart. */
+int fl_vocab_exchange_set_wait_limit(int64_t ns, int64_t* previous);
 
 /* ------------------------------------------------------------------------
  * The single-rank (G = 1) fl_lse_vocab_exchange without any device

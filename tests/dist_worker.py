@@ -94,6 +94,10 @@ def main():
     assert torch.equal(fin_g, torch.isfinite(xs.grad)), "vocab-shard backward: special values differ"
     gerr = (xs.grad[fin_g] - want_g[fin_g]).abs().max().item()
     assert gerr <= 1e-6 + 1e-5 * want_g[fin_g].abs().max().item(), f"vocab-shard backward err {gerr}"
+    # the exchange buffers are CUDA IPC allocations: every rank unmaps its
+    # peers' buffers, then (after a barrier inside close) frees its own
+    for e in (ex, ex32, ex_g):
+        e.close()
     # batch rows
     xb = W.fp32_rows(1000, 20000, seed=5, device=dev)
     r0, r1 = D.local_rows(xb.size(0))

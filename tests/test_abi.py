@@ -56,13 +56,40 @@ def test_version_and_error_without_gpu():
     assert _lib.lib().fl_lse_f32_fwd(None, None, 0, 0, 1, None) == _lib.FL_OK  # empty is a no-op
 
 
-def test_library_is_sm100a_only():
+def test_row_counts_checked_before_arithmetic():
+    """A row count so large that a byte count formed from it would wrap around
+    is rejected before any CUDA call (no GPU needed)."""
     from fuselse_b200 import _lib
-    r = subprocess.run(["cuobjdump", "--list-elf", str(_lib.LIB_PATH)], capture_output=True, text=True)
-    if r.returncode != 0:
-        pytest.skip("cuobjdump unavailable")
-    arches = set(re.findall(r"sm_(\d+a?)", r.stdout))
-    assert arches == {"100a"}, arches
+    L = _lib.lib()
+    fp = ctypes.cast(ctypes.c_void_p(256), ctypes.POINTER(ctypes.c_float))
+    for B in ((1 << 60) + 8, (1 << 59), (1 << 62) + 1):
+        st = L.fl_lse_vocab_exchange_noalloc(ctypes.c_void_p(256), 0, B, 4, fp, None)
+        assert st == _lib.FL_ERR_INVALID_ARGUMENT
+        assert b"at most 262112 rows" in L.fl_last_error()
+    nbytes = ctypes.c_int64()
+    assert L.fl_vocab_exchange_bytes(8, (1 << 60) + 8, ctypes.byref(nbytes)) == _lib.FL_ERR_INVALID_ARGUMENT
+    assert L.fl_vocab_exchange_bytes(8, 8192, ctypes.byref(nbytes)) == _lib.FL_OK
+    assert nbytes.value == 512 + 2 * 8 * 8192 * 8
+
+
+def test_exchange_wait_limit_setter_without_gpu():
+    from fuselse_b200 import _lib
+    L = _lib.lib()
+    prev = ctypes.c_int64()
+    assert L.fl_vocab_exchange_set_wait_limit(100, ctypes.byref(prev)) == _lib.FL_ERR_INVALID_ARGUMENT
+    assert L.fl_vocab_exchange_set_wait_limit(50_000_000, ctypes.byref(prev)) == _lib.FL_OK
+    assert prev.value == 2_000_000_000
+    assert L.fl_vocab_exchange_set_wait_limit(prev.value, None) == _lib.FL_OK
+
+
+@pytest.mark.gpu
+def test_library_kernels_are_sm100():
+    """The kernels the library loads on the GPU were built for sm_100
+    (cudaFuncGetAttributes' binaryVersion; the build targets sm_100a only)."""
+    from fuselse_b200 import _lib
+    v = ctypes.c_int()
+    _lib.call("fl_binary_version", 0, ctypes.byref(v))
+    assert v.value == 100, v.value
 
 
 def test_sparse_bwd_workspace_checks_without_gpu():
