@@ -39,22 +39,27 @@ def make_fuselse_logsumexp(extension=None, robust: bool = True):
         "logsumexp_dim", "logsumexp_dim_backward"))
     reference_logsumexp = torch.logsumexp
 
-    class FuseLSEFunction(torch.autograd.Function):
-        @staticmethod
-        def forward(ctx, input_tensor):
-            row_size = input_tensor.shape[-1]
-            flat_input = input_tensor.reshape(-1, row_size).contiguous()
-            output = forward_kernel(flat_input)
-            ctx.save_for_backward(flat_input, output)
-            ctx.input_shape = tuple(input_tensor.shape)
-            return output.reshape(input_tensor.shape[:-1])
+    def dense_rows(t):
+        """(..., N) as a dense (R, N) matrix — a view when the rows already are
+        dense, else the copy the reference makes — and the leading shape."""
+        return t.reshape(-1, t.shape[-1]).contiguous(), t.shape[:-1]
+
+    class DenseRowsLSE(torch.autograd.Function):
+        """Last-dim reduction over dense rows.  Keeps the (R, N) rows and their
+        lse for the backward, which is one fused pass g * exp(x - lse)."""
 
         @staticmethod
-        def backward(ctx, grad_output):
-            flat_input, output = ctx.saved_tensors
-            flat_grad = grad_output.reshape(-1).contiguous()
-            grad_input = backward_kernel(flat_grad, flat_input, output)
-            return grad_input.reshape(ctx.input_shape)
+        def forward(ctx, t):
+            rows, lead = dense_rows(t)
+            lse = forward_kernel(rows)
+            ctx.save_for_backward(rows, lse)
+            ctx.shape = t.shape
+            return lse.view(lead)
+
+        @staticmethod
+        def backward(ctx, g):
+            rows, lse = ctx.saved_tensors
+            return backward_kernel(g.reshape(-1).contiguous(), rows, lse).view(ctx.shape)
 
     class FuseLSEStridedFunction(torch.autograd.Function):
         """Last-dim reduction of a strided input, read in place (no copy)."""
@@ -110,14 +115,11 @@ def make_fuselse_logsumexp(extension=None, robust: bool = True):
             result = (FuseLSEStridedFunction.apply(input_tensor) if grad
                       else extension.onepass_lse_float_strided(input_tensor, robust=robust))
         elif grad:
-            result = FuseLSEFunction.apply(input_tensor)
-        elif input_tensor.dim() == 2 and input_tensor.is_contiguous():
-            result = forward_kernel(input_tensor)
-        else:
-            row_size = input_tensor.shape[-1]
-            flat_input = input_tensor.reshape(-1, row_size).contiguous()
-            result = forward_kernel(flat_input).reshape(input_tensor.shape[:-1])
+            result = DenseRowsLSE.apply(input_tensor)
+        else:  # no graph: a dense 2-D input goes to the kernel as it is
+            rows, lead = dense_rows(input_tensor)
+            result = forward_kernel(rows).view(lead)
         return result.unsqueeze(-1) if keepdim else result
 
-    logsumexp.FuseLSEFunction = FuseLSEFunction
+    logsumexp.autograd_function = DenseRowsLSE
     return logsumexp

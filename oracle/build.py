@@ -27,7 +27,9 @@ HERE = Path(__file__).resolve().parent
 BUILD = HERE / "_build"
 REF_OUT = HERE / "_ref"
 ORACLE_SO = BUILD / "liblse_oracle.so"
-REF_SRC = Path(os.environ.get("FUSELSE_REFERENCE", "/root/reference"))
+# the reference checkout: FUSELSE_REFERENCE, else a `reference` directory
+# beside this repository's root
+REF_SRC = Path(os.environ.get("FUSELSE_REFERENCE", HERE.parent.parent / "reference"))
 
 # reference GPU sources -> extension module names
 REF_CUDA = {
