@@ -87,6 +87,23 @@ __device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
     return v;
 }
 
+// L2 eviction-priority policy for loads whose lines are not read again.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t p;
+    asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// ld_stream_u4 with an L2 cache policy (createpolicy) for the lines it brings in.
+__device__ __forceinline__ uint4 ld_stream_u4_policy(const void* p, uint64_t policy) {
+    uint4 v;
+    asm volatile(
+        "ld.global.nc.L1::no_allocate.L2::cache_hint.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+        : "l"(p), "l"(policy));
+    return v;
+}
+
 // 16-byte store that marks the lines evict-first in L2 (written once).
 __device__ __forceinline__ void st_stream_f4(void* p, float4 v) {
     asm volatile("st.global.cs.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p),
@@ -122,6 +139,88 @@ __device__ __forceinline__ float ex2_poly(float t) {
     p = fmaf(p, f, 0.6931469440460205f);
     p = fmaf(p, f, 1.0000001192092896f);
     return __int_as_float(__float_as_int(p) + (__float_as_int(j) << 23));
+}
+
+// Split cluster barrier.  A CTA must not touch another CTA's shared memory
+// before that CTA is known to have started: each CTA arrives (relaxed: no
+// memory ordering is needed for that) at its start and waits just before its
+// first distributed-shared-memory access, so the barrier's latency hides
+// behind the work in between.  Every thread of the cluster executes both.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+}
+
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialization may start while the kernel before it in the stream is still
+// running; pdl_wait() blocks until that kernel has completed and its memory
+// is visible (a no-op when the launch had no such dependency), so every
+// global access after it is ordered exactly as in plain stream order.
+// pdl_launch_dependents() lets the next kernel's CTAs be scheduled early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Global nanosecond timer (bounds every wait in this library's kernels).
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier + 1-D bulk copy (global -> this CTA's shared memory) helpers.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+// Makes initialised barriers visible to the bulk-copy (async) proxy.
+__device__ __forceinline__ void mbar_init_fence() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+// Waits for the phase of parity `parity` to complete; false after ~`limit_ns`.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  uint64_t limit_ns = 1000000000ull) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 63u) == 0 && global_ns() - t0 > limit_ns) return false;
+    }
+}
+// cp.async.bulk global -> shared of this CTA, completing `bytes` of tx on
+// `bar`.  dst, src 16-byte aligned; bytes a multiple of 16.  This CTA only.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
 }
 
 // max that propagates NaN (PTX max.NaN.f32, sm_80+).

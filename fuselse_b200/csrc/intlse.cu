@@ -152,6 +152,9 @@ __global__ void __launch_bounds__(CTA) intlse_rows_kernel(
     const int rank = C > 1 ? static_cast<int>(blockIdx.x % C) : 0;
     const int lane = threadIdx.x & 31;
     const int t = rank * CTA + threadIdx.x;
+    // C > 1: the grid holds exactly one row per cluster, so every CTA below
+    // runs the row loop once and reaches the wait before its DSMEM store
+    if constexpr (C > 1) cluster_arrive_relaxed();
 
     if constexpr (LUT) {
         fill_lane_lut<CTA>(lut_s, F == 16 ? kLutQ16 : kLutQ10_6);
@@ -232,6 +235,7 @@ __global__ void __launch_bounds__(CTA) intlse_rows_kernel(
 
         if constexpr (C > 1) {
             cg::cluster_group cluster = cg::this_cluster();
+            cluster_wait();  // rank 0 has started: its warp_val exists
             if (lane == 0) {
                 int* dst = cluster.map_shared_rank(warp_val, 0);
                 dst[t >> 5] = acc;

@@ -25,6 +25,7 @@
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
 
 namespace cg = cooperative_groups;
@@ -87,6 +88,9 @@ __global__ void __launch_bounds__(FwdShape<T>::kThreads) lse_segment_kernel(
     const int rank = static_cast<int>(blockIdx.x % nseg);
     const int64_t row = blockIdx.x / nseg;
     __shared__ float2 seg_part[kMaxSeg];
+    if (nseg > 1) cluster_arrive_relaxed();
+    pdl_wait();
+    pdl_launch_dependents();
 
     float m = -INFINITY, s = 0.0f;
     Target<T> tg;
@@ -108,6 +112,7 @@ __global__ void __launch_bounds__(FwdShape<T>::kThreads) lse_segment_kernel(
     }
     ms_block_reduce<FwdShape<T>::kThreads>(m, s);
     if (nseg > 1) {
+        cluster_wait();  // rank 0 has started: its seg_part exists
         if (threadIdx.x == 0) {
             float2* dst = cluster.map_shared_rank(seg_part, 0);
             dst[rank] = make_float2(m, s);
@@ -123,6 +128,128 @@ __global__ void __launch_bounds__(FwdShape<T>::kThreads) lse_segment_kernel(
     if (threadIdx.x == 0 && row < B) write_row<T, MODE>(out, row, m, s, empty_value, tg, sel);
 }
 
+// Long dense rows staged through shared memory: one CTA per row, its thread 0
+// streaming the row's 16-byte-aligned body into a ring of kBulkStages buffers
+// of 16 KB with 1-D bulk copies (cp.async.bulk, completion counted in bytes on
+// one mbarrier per buffer), all threads folding each buffer from shared
+// memory and releasing it through a second mbarrier (one arrival per warp)
+// before thread 0 refills it.  The bytes in flight per CTA are the ring, not
+// the loads a thread can hold in registers.  Head and tail elements (before
+// the first / after the last 16-byte boundary) are read directly.  Every wait
+// is bounded (~1 s): a row whose copies never complete gives NaN and bumps
+// *err_count, after thread 0 has waited (bounded) for the copies it issued.
+#ifndef FL_FWD_BULK
+#define FL_FWD_BULK 0
+#endif
+#ifndef FL_BULK_STAGES
+#define FL_BULK_STAGES 3
+#endif
+constexpr int kBulkThreads = 256;
+constexpr int kBulkStages = FL_BULK_STAGES;
+constexpr int kBulkStageBytes = 16384;
+constexpr int kBulkStageVecs = kBulkStageBytes / 16;
+constexpr int kBulkVecsPerThread = kBulkStageVecs / kBulkThreads;  // 4
+constexpr int kBulkSmem = kBulkStages * kBulkStageBytes;
+
+__device__ int g_bulk_wait_errors;  // rows given up on (copies never completed)
+
+template <typename T, int MODE>
+__global__ void __launch_bounds__(kBulkThreads, 4) lse_bulk_kernel(
+    const T* __restrict__ x, float* __restrict__ out, int64_t B, int64_t N,
+    float empty_value, SelArgs sel, RowMap rm) {
+    constexpr int E = Elem<T>::kPerVec;
+    extern __shared__ __align__(128) unsigned char ring[];
+    __shared__ uint64_t full[kBulkStages], empty[kBulkStages];
+    const int64_t row = blockIdx.x;
+    const int lane = threadIdx.x & 31;
+    const T* rowp = x + rm(row);
+    const int64_t head = head_elems(rowp, N);
+    const int64_t nv = (N - head) / E;
+    const int64_t tail0 = head + nv * E;
+    const unsigned char* body = reinterpret_cast<const unsigned char*>(rowp + head);
+    const int64_t nstage = (nv + kBulkStageVecs - 1) / kBulkStageVecs;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kBulkStages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kBulkThreads / 32);
+        }
+        mbar_init_fence();
+    }
+    __syncthreads();
+    pdl_wait();
+    pdl_launch_dependents();
+    int64_t issued = 0;  // thread 0 only
+    auto issue = [&](int64_t k) {
+        const int slot = static_cast<int>(k % kBulkStages);
+        const int64_t v0 = k * kBulkStageVecs;
+        const uint32_t bytes = static_cast<uint32_t>(min(nv - v0, (int64_t)kBulkStageVecs) * 16);
+        mbar_arrive_expect_tx(&full[slot], bytes);
+        bulk_load(ring + slot * kBulkStageBytes, body + v0 * 16, bytes, &full[slot]);
+        issued = k + 1;
+    };
+    if (threadIdx.x == 0)
+        for (int64_t k = 0; k < nstage && k < kBulkStages; ++k) issue(k);
+
+    Target<T> tg;
+    if (MODE == kOutSelect && threadIdx.x == 0) tg.fetch(rowp, N, row, sel);
+    float m = -INFINITY, s = 0.0f;
+    // head / tail elements overlap the first copies
+    if (threadIdx.x < head) ms_fold1(m, s, Elem<T>::load1(rowp + threadIdx.x));
+    if (tail0 + threadIdx.x < N) ms_fold1(m, s, Elem<T>::load1(rowp + tail0 + threadIdx.x));
+
+    bool ok = true;
+    int64_t k = 0;
+    for (; k < nstage; ++k) {
+        const int slot = static_cast<int>(k % kBulkStages);
+        const uint32_t parity = static_cast<uint32_t>((k / kBulkStages) & 1);
+        if (!mbar_wait_bounded(&full[slot], parity)) {
+            ok = false;
+            break;
+        }
+        const uint4* sv = reinterpret_cast<const uint4*>(ring + slot * kBulkStageBytes);
+        const int64_t left = nv - k * kBulkStageVecs;
+        if (left >= kBulkStageVecs) {
+            float v[kBulkVecsPerThread * E];
+#pragma unroll
+            for (int u = 0; u < kBulkVecsPerThread; ++u)
+                Elem<T>::unpack(sv[threadIdx.x + u * kBulkThreads], v + u * E);
+            ms_fold<kBulkVecsPerThread * E, FwdShape<T>::kPoly>(m, s, v);
+        } else {
+            for (int i = threadIdx.x; i < left; i += kBulkThreads) {
+                float v[E];
+                Elem<T>::unpack(sv[i], v);
+                ms_fold<E, FwdShape<T>::kPoly>(m, s, v);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        if (threadIdx.x == 0 && k + kBulkStages < nstage) {
+            if (!mbar_wait_bounded(&empty[slot], parity)) {
+                ok = false;
+                break;
+            }
+            issue(k + kBulkStages);
+        }
+    }
+    if (!ok && threadIdx.x == 0) {
+        // do not leave the CTA while a copy it issued may still land in its
+        // shared memory: wait (bounded) for every issued stage not yet consumed
+        for (int64_t j = k; j < issued; ++j)
+            mbar_wait_bounded(&full[j % kBulkStages], static_cast<uint32_t>((j / kBulkStages) & 1));
+        atomicAdd(&g_bulk_wait_errors, 1);
+    }
+    const int bad = __syncthreads_or(!ok);
+    ms_block_reduce<kBulkThreads>(m, s);
+    if (threadIdx.x == 0) {
+        if (bad) {
+            m = __int_as_float(0x7fc00000);
+            s = 0.0f;
+        }
+        write_row<T, MODE>(out, row, m, s, empty_value, tg, sel);
+    }
+}
+
 // One warp per row for short rows.
 template <typename T, int MODE>
 __global__ void __launch_bounds__(kThreads) lse_warp_kernel(
@@ -130,6 +257,8 @@ __global__ void __launch_bounds__(kThreads) lse_warp_kernel(
     float empty_value, SelArgs sel, RowMap rm) {
     const int lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+    pdl_wait();
+    pdl_launch_dependents();
     if (row >= B) return;
     const T* rowp = x + rm(row);
     Target<T> tg;
@@ -158,14 +287,27 @@ __global__ void lse_combine_kernel(const float2* __restrict__ ms, float* __restr
 // A row whose x and gx starts differ in 16-byte phase (possible for strided x)
 // is done with 4-byte accesses over the same chunk split.
 constexpr int kBwdUnroll = 4;
+#ifndef FL_BWD_ORDER
+#define FL_BWD_ORDER 0
+#endif
+#ifndef FL_BWD_X_EVICT_FIRST
+#define FL_BWD_X_EVICT_FIRST 0
+#endif
 
 template <bool SEL>
 __global__ void __launch_bounds__(kThreads) lse_bwd_kernel(
     const float* __restrict__ g, const float* __restrict__ x,
     const float* __restrict__ lse, float* __restrict__ gx, int64_t B, int64_t N,
     int nchunk, int64_t chunk_vec, const int64_t* __restrict__ index, RowMap rm) {
+#if FL_BWD_ORDER == 1
+    const int64_t row = static_cast<int64_t>(blockIdx.x % B);
+    const int chunk = nchunk - 1 - static_cast<int>(blockIdx.x / B);
+#else
     const int chunk = static_cast<int>(blockIdx.x % nchunk);
     const int64_t row = static_cast<int64_t>(blockIdx.x / nchunk);
+#endif
+    pdl_wait();
+    pdl_launch_dependents();
     const float* xr = x + rm(row);
     float* gr = gx + row * N;
     const float g0 = __ldg(g + row);
@@ -209,19 +351,58 @@ __global__ void __launch_bounds__(kThreads) lse_bwd_kernel(
         return o;
     };
     int64_t i = v0 + threadIdx.x;
+#if FL_BWD_X_EVICT_FIRST
+    const uint64_t pol = l2_policy_evict_first();
+#define FL_BWD_LD(p) ld_stream_u4_policy(p, pol)
+#else
+#define FL_BWD_LD(p) ld_stream_u4(p)
+#endif
     for (; i + (kBwdUnroll - 1) * kThreads < v1; i += kBwdUnroll * kThreads) {
         uint4 r[kBwdUnroll];
 #pragma unroll
-        for (int u = 0; u < kBwdUnroll; ++u) r[u] = ld_stream_u4(xv + i + u * kThreads);
+        for (int u = 0; u < kBwdUnroll; ++u) r[u] = FL_BWD_LD(xv + i + u * kThreads);
 #pragma unroll
         for (int u = 0; u < kBwdUnroll; ++u) st_stream_f4(gv + i + u * kThreads, vec(r[u], i + u * kThreads));
     }
-    for (; i < v1; i += kThreads) st_stream_f4(gv + i, vec(ld_stream_u4(xv + i), i));
+    for (; i < v1; i += kThreads) st_stream_f4(gv + i, vec(FL_BWD_LD(xv + i), i));
+#undef FL_BWD_LD
 }
 
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
+// Launch configuration of the row kernels: programmatic stream serialization
+// (the kernel may be scheduled while its predecessor in the stream drains;
+// it orders itself with pdl_wait before touching memory), plus an optional
+// cluster shape.
+#ifndef FL_PDL
+#define FL_PDL 1
+#endif
+struct LaunchCfg {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[2];
+    LaunchCfg(dim3 grid, dim3 block, size_t smem, cudaStream_t stream) {
+        cfg.gridDim = grid;
+        cfg.blockDim = block;
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = stream;
+        cfg.attrs = attr;
+        cfg.numAttrs = 0;
+        if (FL_PDL) {
+            attr[cfg.numAttrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[cfg.numAttrs].val.programmaticStreamSerializationAllowed = 1;
+            ++cfg.numAttrs;
+        }
+    }
+    void cluster(int n) {
+        attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
+        attr[cfg.numAttrs].val.clusterDim.x = n;
+        attr[cfg.numAttrs].val.clusterDim.y = 1;
+        attr[cfg.numAttrs].val.clusterDim.z = 1;
+        ++cfg.numAttrs;
+    }
+};
+
 int env_int(const char* name, int dflt) {
     const char* v = std::getenv(name);
     if (!v || !*v) return dflt;
@@ -263,25 +444,31 @@ int launch_rows(const T* x, float* out, int64_t B, int64_t N, float empty_value,
     if (warp_per_row<T>(B, N)) {
         const int64_t grid = (B + kWarps - 1) / kWarps;
         FL_REQUIRE(grid <= INT32_MAX, "%s: B=%lld too large", what, (long long)B);
-        lse_warp_kernel<T, MODE><<<(unsigned)grid, kThreads, 0, stream>>>(x, out, B, N, empty_value, sel, rm);
+        LaunchCfg lc(dim3((unsigned)grid), dim3(kThreads), 0, stream);
+        FL_CUDA(cudaLaunchKernelEx(&lc.cfg, lse_warp_kernel<T, MODE>, x, out, B, N, empty_value, sel, rm));
         return check_launch(what);
     }
     const int nseg = choose_nseg<T>(B, N);
+    if (FL_FWD_BULK && nseg == 1 && N * (int64_t)sizeof(T) >= 4 * kBulkStageBytes) {
+        static std::atomic<uint64_t> configured{0};  // one bit per device
+        int dev = 0;
+        FL_CUDA(cudaGetDevice(&dev));
+        const uint64_t bit = 1ull << (dev & 63);
+        if (!(configured.load(std::memory_order_relaxed) & bit)) {
+            FL_CUDA(cudaFuncSetAttribute(lse_bulk_kernel<T, MODE>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kBulkSmem));
+            configured.fetch_or(bit, std::memory_order_relaxed);
+        }
+        FL_REQUIRE(B <= INT32_MAX, "%s: B=%lld too large", what, (long long)B);
+        LaunchCfg lc(dim3((unsigned)B), dim3(kBulkThreads), kBulkSmem, stream);
+        FL_CUDA(cudaLaunchKernelEx(&lc.cfg, lse_bulk_kernel<T, MODE>, x, out, B, N, empty_value, sel, rm));
+        return check_launch(what);
+    }
     const int64_t grid = B * nseg;
     FL_REQUIRE(grid <= INT32_MAX, "%s: B=%lld too large", what, (long long)B);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(FwdShape<T>::kThreads);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = nseg;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    FL_CUDA(cudaLaunchKernelEx(&cfg, lse_segment_kernel<T, MODE>, x, out, B, N, nseg,
+    LaunchCfg lc(dim3((unsigned)grid), dim3(FwdShape<T>::kThreads), 0, stream);
+    lc.cluster(nseg);
+    FL_CUDA(cudaLaunchKernelEx(&lc.cfg, lse_segment_kernel<T, MODE>, x, out, B, N, nseg,
                                empty_value, sel, rm));
     return check_launch(what);
 }
@@ -388,13 +575,19 @@ int launch_bwd(const float* g, const float* x, const float* lse, const int64_t* 
                "%s: misaligned buffer", what);
     if (int st = bind_device(stream, gx)) return st;
     const int64_t nv = N / 4 + 1;
-    // ~64 KB of x per CTA
-    const int64_t chunk_vec = 4096;
+    // 16 KB of x per CTA (one unrolled pass of its 256 threads): many short
+    // CTAs keep the end of the grid balanced (64 KB chunks measured 4 us
+    // slower on the (512, 128256) backward)
+#ifndef FL_BWD_CHUNK_VEC
+#define FL_BWD_CHUNK_VEC 1024
+#endif
+    const int64_t chunk_vec = FL_BWD_CHUNK_VEC;
     const int64_t nchunk = (nv + chunk_vec - 1) / chunk_vec;
     const int64_t grid = B * nchunk;
     FL_REQUIRE(grid <= INT32_MAX, "%s: B*N too large", what);
-    lse_bwd_kernel<SEL><<<(unsigned)grid, kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        g, x, lse, gx, B, N, (int)nchunk, chunk_vec, index, rm);
+    LaunchCfg lc(dim3((unsigned)grid), dim3(kThreads), 0, reinterpret_cast<cudaStream_t>(stream));
+    FL_CUDA(cudaLaunchKernelEx(&lc.cfg, lse_bwd_kernel<SEL>, g, x, lse, gx, B, N, (int)nchunk,
+                               chunk_vec, index, rm));
     return check_launch(what);
 }
 
