@@ -14,14 +14,21 @@ ranks / max-over-ranks device time.
 Algorithmic bytes per step and GPU (the roofline numerator):
   forward  B*N*4 + B*4                = 262,670,336 B
   backward 2*B*N*4 + 2*B*4            = 525,340,672 B  (read x, g, lse; write gx)
-Timing: W untimed warm-up steps; K timed steps, each kernel replayed from its
-own CUDA graph (captured once through the public entry points; `--eager` calls
-them directly) and bracketed by CUDA events on the launching stream (forward
-and backward separately), steps back to back
-with inputs larger than L2 (x and gx are 262 MB each, L2 126 MB; each kernel
-pays the write-back of the previous kernel's dirty lines, as in a training
-loop); `--flush-l2` instead evicts L2 between steps outside the events; barrier and
-synchronize around the timed region; max over ranks.
+Timing: W untimed warm-up steps, then two timed passes of K steps each, steps
+back to back, with inputs larger than L2 (x and gx are 262 MB each, L2 126 MB;
+each kernel pays the write-back of the previous kernel's dirty lines, as in a
+training loop) and two input batches alternating step by step, so no step
+finds its input left in L2 by the step before (`--same-input`: one batch);
+`--flush-l2` instead evicts L2 between steps outside the events.
+  * step pass (`value`, `ms_per_step`): each step — forward then backward — is
+    one CUDA graph captured through the public entry points, replayed K times
+    between two CUDA events on the launching stream (as a training loop that
+    captures its step runs it);
+  * per-kernel pass (`kernels`, `roofline`): each kernel replayed from its own
+    graph with CUDA events between the kernels (`ms_per_step_kernel_pass` is
+    their sum; `--kernel-graphs` reports it as the step, `--eager` launches
+    directly).
+Barrier and synchronize around each timed region; max over ranks.
 
 `e2e` (default workload): the same metric through the public host-buffer API
 (fuselse_b200.host.HostRowPipeline): every step x and g are copied in from
@@ -151,21 +158,33 @@ class Workload:
 
 
 class FwdBwdF32(Workload):
+    """Steps alternate between two input batches (x0, x1), so a step never
+    finds its input left in L2 by the step before; within a step the backward
+    reads the same x as the forward, as a training step does."""
     name = "fwdbwd_f32"
     dtype = "f32"
 
-    def __init__(self, dev, seed, B=B_ROWS, N=N_COLS, do_bwd=True):
+    def __init__(self, dev, seed, B=B_ROWS, N=N_COLS, do_bwd=True, same_input=False):
         from fuselse_b200 import ext, workloads as W
         self.ext, self.B, self.N, self.do_bwd = ext, B, N, do_bwd
-        self.x = W.fp32_rows(B, N, seed, dev)
+        self.xs = [W.fp32_rows(B, N, seed, dev)]
+        if not same_input:
+            self.xs.append(W.fp32_rows(B, N, seed + 1000, dev))
+        self.phases = len(self.xs)
+        self.x = self.xs[0]
         self.g = torch.ones(B, device=dev)
         self.lse = torch.empty(B, device=dev)
+        inputs = ("one input batch every step" if same_input else
+                  "two input batches alternating step by step (no input reused from L2 across steps)")
         self.config = {"workload": f"FuseLSE fp32 {'forward+backward' if do_bwd else 'forward'} "
                                    f"(B,N)=({B},{N}) per GPU, x~N(0,1), grad ones, robust",
                        "B": B, "N": N,
-                       "l2": "inputs larger than L2 (x 262 MB, gx 262 MB), steps back to back",
+                       "l2": f"inputs larger than L2 (x 262 MB, gx 262 MB), steps back to back, {inputs}",
                        "parallelism": "batch rows, one process per GPU, no collective"}
         self.launches_per_step = 2 if do_bwd else 1
+
+    def set_phase(self, p):
+        self.x = self.xs[p % self.phases]
 
     def _fwd(self):
         self.lse = self.ext.onepass_lse_float_robust(self.x)
@@ -279,6 +298,136 @@ class F16Vocab(Workload):
         return self.B
 
 
+class VocabSplit(Workload):
+    """BASELINE's LLM-logit configuration split across the job: fp16 logits
+    (8192, 128256) cut into `world` contiguous vocab shards, one per GPU (8 x
+    16032 at 8 GPUs; the whole row on one GPU), every rank ending with the
+    full (8192,) lse.  mode "nvlink": the library's exchange (fold + pair
+    stores into every rank's buffer over NVLink + flag-wait combine, one
+    call); mode "nccl": lse_partial, an NCCL all-gather of the (B, 2) pairs,
+    lse_combine, timed separately; mode "fold": lse_partial alone (the
+    shard's fold, no exchange)."""
+    name = "vocab_split"
+    dtype = "f16"
+    B, V = 8192, 128256
+
+    def __init__(self, dev, world, rank, mode, parts=None):
+        from fuselse_b200 import distributed as D, ext, workloads as W
+        self.ext, self.world, self.mode = ext, world, mode
+        parts = parts or world
+        full = W.fp16_logits(self.B, self.V, seed=0, device=dev)  # identical on every rank
+        self.xs = W.vocab_shard(full, parts, rank % parts)
+        del full
+        torch.cuda.empty_cache()
+        self.Ns = self.xs.size(1)
+        self.ex = None
+        if mode == "nvlink":
+            self.ex = (D.VocabShardExchange(self.B, device=dev) if world > 1
+                       else D.VocabShardExchange.single_rank(self.B, dev))
+        self.launches_per_step = {"nvlink": 2, "nccl": 2, "fold": 1}[mode]
+
+    def _exchange(self):
+        self.out = self.ex(self.xs)
+
+    def _partial(self):
+        self.ms = self.ext.lse_partial(self.xs)
+
+    def _gather(self):
+        from fuselse_b200 import distributed as D
+        self.allms = D.gather_partials(self.ms) if self.world > 1 else self.ms.unsqueeze(0)
+
+    def _combine(self):
+        self.out = self.ext.lse_combine(self.allms)
+
+    def _combine1(self):
+        self.out = self.ext.lse_combine(self.ms.unsqueeze(0))
+
+    def kernels(self):
+        shard = self.B * self.Ns * 2 + self.B * 4
+        if self.mode == "nvlink":
+            return [("exchange", self._exchange, shard)]
+        if self.mode == "fold":
+            return [("fold", self._partial, shard)]
+        if self.world == 1:  # nothing to gather: the combine reads the one partial
+            return [("partial", self._partial, shard), ("combine", self._combine1, 0)]
+        return [("partial", self._partial, shard), ("all_gather", self._gather, 0),
+                ("combine", self._combine, 0)]
+
+    def close(self):
+        if self.ex is not None and self.world > 1:
+            self.ex.close()
+        self.ex = None
+
+    def rows(self):
+        return self.B
+
+
+def vocab_exchange_record(dev, world, rank, steps, warmup, dist_on):
+    """The `vocab_exchange` key: BASELINE config 3 over `world` GPUs through the
+    NVLink exchange and through the NCCL all-gather, with the shard's fold
+    timed alone, and the whole (8192, 128256) on one GPU (t1) for reference."""
+    total_bytes = VocabSplit.B * VocabSplit.V * 2 + VocabSplit.B * 4
+    rec = {"config": "FuseLSE16 fp16 logits (8192,128256) x~N(0,3^2)+15 spike, split into "
+                     f"{world} contiguous vocab shards of ~{-(-VocabSplit.V // world)} columns, "
+                     "full lse on every rank",
+           "algorithmic_bytes": total_bytes}
+    out = {}
+    for mode in ("fold", "nvlink", "nccl"):
+        wl = VocabSplit(dev, world, rank, mode)
+        _, per = run_timed(wl, steps, warmup, dev, dist_on)
+        ms = run_step_graphs(wl, steps, warmup, dev, dist_on)
+        wl.close()
+        per = [max_over_ranks(v, dist_on, dev) for v in per]
+        ms = max_over_ranks(ms, dist_on, dev)
+        labels = [lab for lab, _, _ in wl.kernels()]
+        out[mode] = (ms, dict(zip(labels, per)))
+        del wl
+        torch.cuda.empty_cache()
+    fold_ms = out["fold"][0]
+    nv_ms = out["nvlink"][0]
+    nc_ms, nc_k = out["nccl"]
+    rec["nvlink"] = {"ms": nv_ms, "GB_s": total_bytes / (nv_ms * 1e-3) / 1e9,
+                     "shard_fold_us": fold_ms * 1e3,
+                     "exchange_combine_us": (nv_ms - fold_ms) * 1e3,
+                     "note": "one call (fold + NVLink pair stores, then flag-wait combine); "
+                             "exchange_combine_us = call time - the shard's fold timed alone"}
+    rec["nccl"] = {"ms": nc_ms, "GB_s": total_bytes / (nc_ms * 1e-3) / 1e9,
+                   "partial_us": nc_k["partial"] * 1e3,
+                   "all_gather_us": nc_k.get("all_gather", 0.0) * 1e3,
+                   "combine_us": nc_k["combine"] * 1e3}
+    if world > 1:
+        # the same logits whole on one GPU (every rank its own copy), for the efficiency
+        wl = VocabSplit(dev, 1, 0, "nvlink", parts=1)
+        t1 = run_step_graphs(wl, steps, warmup, dev, dist_on)
+        wl.close()
+        del wl
+        torch.cuda.empty_cache()
+        t1 = max_over_ranks(t1, dist_on, dev)
+        rec["t1_ms"] = t1
+        rec["nvlink"]["efficiency_vs_1gpu"] = t1 / (world * nv_ms)
+        rec["nccl"]["efficiency_vs_1gpu"] = t1 / (world * nc_ms)
+    return rec
+
+
+def strong_record(dev, world, rank, steps, warmup, dist_on, t1_ms):
+    """The `strong` key: the headline's 512 rows split over the job's GPUs
+    (64 rows each at 8 GPUs: rows split into cluster segments), forward +
+    backward per step, max over ranks; t1_ms = this run's own 512-row step."""
+    from fuselse_b200.distributed import split_range
+    lo, hi = split_range(B_ROWS, world, rank)
+    wl = FwdBwdF32(dev, seed=rank, B=hi - lo)
+    ms = run_step_graphs(wl, steps, warmup, dev, dist_on)
+    ms = max_over_ranks(ms, dist_on, dev)
+    del wl
+    torch.cuda.empty_cache()
+    total = 3 * B_ROWS * N_COLS * 4 + 3 * B_ROWS * 4
+    return {"config": f"FuseLSE fp32 fwd+bwd (512,128256) split over {world} GPU(s), "
+                      f"{hi - lo} rows on rank {rank}",
+            "ms_per_step": ms, "rows_per_s": B_ROWS / (ms * 1e-3),
+            "GB_s": total / (ms * 1e-3) / 1e9, "t1_ms": t1_ms,
+            "efficiency_vs_1gpu": t1_ms / (world * ms)}
+
+
 class IntLSE(Workload):
     dtype = "int32"
 
@@ -384,11 +533,11 @@ class SparseFwdBwd(Workload):
         return self.args[4].size(0)
 
 
-def make_workload(name, dev, seed, world, rank):
+def make_workload(name, dev, seed, world, rank, same_input=False):
     if name == "fwdbwd_f32":
-        return FwdBwdF32(dev, seed)
+        return FwdBwdF32(dev, seed, same_input=same_input)
     if name == "fwd_f32":
-        return FwdBwdF32(dev, seed, do_bwd=False)
+        return FwdBwdF32(dev, seed, do_bwd=False, same_input=same_input)
     if name == "sls_f32":
         return SelectiveF32(dev, seed)
     if name == "f16_vocab":
@@ -454,15 +603,24 @@ def capture_graphs(fns, warmup):
 def run_timed(wl, steps, warmup, dev, dist_on, flush_l2=False, graphs=True):
     """Steps back to back (inputs larger than L2), or with an untimed L2Flush
     between steps; every kernel launched from its own CUDA graph (host
-    overhead off the device timeline) with CUDA events between them."""
+    overhead off the device timeline) with CUDA events between them.  A
+    workload with `phases` > 1 input batches cycles through them, step k
+    running on batch k % phases."""
     flush = L2Flush(dev) if flush_l2 else (lambda: None)
-    ks = wl.kernels()
-    held = []
-    if graphs:
-        fns, held = capture_graphs([fn for _, fn, _ in ks], warmup)
-        ks = [(lab, f, b) for (lab, _, b), f in zip(ks, fns)]
-    for _ in range(warmup):
-        for _, fn, _ in ks:
+    phases = getattr(wl, "phases", 1)
+    sets, held = [], []
+    for p in range(phases):
+        if phases > 1:
+            wl.set_phase(p)
+        ks = wl.kernels()
+        if graphs:
+            fns, gs = capture_graphs([fn for _, fn, _ in ks], warmup)
+            held += gs
+            ks = [(lab, f, b) for (lab, _, b), f in zip(ks, fns)]
+        sets.append(ks)
+    ks = sets[0]
+    for w in range(warmup):
+        for _, fn, _ in sets[w % phases]:
             fn()
     torch.cuda.synchronize()
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(ks) + 1)] for _ in range(steps)]
@@ -472,7 +630,7 @@ def run_timed(wl, steps, warmup, dev, dist_on, flush_l2=False, graphs=True):
     for k in range(steps):
         flush()
         evs[k][0].record()
-        for i, (_, fn, _) in enumerate(ks):
+        for i, (_, fn, _) in enumerate(sets[k % phases]):
             fn()
             evs[k][i + 1].record()
     torch.cuda.synchronize()
@@ -483,6 +641,56 @@ def run_timed(wl, steps, warmup, dev, dist_on, flush_l2=False, graphs=True):
     step_ms = sum(per_kernel)
     held.clear()  # graphs holding NCCL calls must go before the process group does
     return step_ms, per_kernel
+
+
+def run_step_graphs(wl, steps, warmup, dev, dist_on, flush_l2=False):
+    """Each step — all of its kernels, in order — replayed from ONE CUDA graph
+    (one per input batch), with CUDA events at step boundaries only; returns
+    the mean step time.  Per-kernel times come from run_timed."""
+    flush = L2Flush(dev) if flush_l2 else (lambda: None)
+    phases = getattr(wl, "phases", 1)
+    steps_fns, held = [], []
+    for p in range(phases):
+        if phases > 1:
+            wl.set_phase(p)
+        ks = wl.kernels()
+
+        def step(ks=ks):
+            for _, fn, _ in ks:
+                fn()
+
+        fns, gs = capture_graphs([step], warmup)
+        held += gs
+        steps_fns.append(fns[0])
+    for w in range(warmup):
+        steps_fns[w % phases]()
+    torch.cuda.synchronize()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    if dist_on:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    if flush_l2:
+        times = []
+        for k in range(steps):
+            flush()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            steps_fns[k % phases]()
+            b.record()
+            times.append((a, b))
+        torch.cuda.synchronize()
+        step_ms = sum(a.elapsed_time(b) for a, b in times) / steps
+    else:
+        evs[0].record()
+        for k in range(steps):
+            steps_fns[k % phases]()
+        evs[steps].record()
+        torch.cuda.synchronize()
+        step_ms = evs[0].elapsed_time(evs[steps]) / steps
+    if dist_on:
+        torch.distributed.barrier()
+    held.clear()
+    return step_ms
 
 
 def run_e2e(wl, steps, warmup, dev, dist_on):
@@ -551,6 +759,53 @@ def cpu_baseline(rows, budget_s=10.0):
             "rows_per_s": rows / per, "cpu": _cpu_name()}
 
 
+def cpu_reference_configs(reps=5):
+    """BASELINE's CPU configuration on this host: (32, 128256) fp32, x ~ N(0, 1)
+    from torch.Generator().manual_seed(0): the reference AVX2 IntLSE
+    (lse_q16_2d_simd, intlse/cpu/lse_kernel_simd.c:232-236, single-threaded by
+    design; "all cores" = rows over a thread pool), the reference FuseLSE-CPU
+    (cpu_lse_float, fuselse/cpu/fused_fp32_cpu.cpp:28-46, at::parallel_for)
+    and torch.logsumexp, each on 1 thread and on all host threads; median of
+    `reps` timed runs after one warm-up (benchmark.py:36-44's form)."""
+    from oracle import oracle as O
+    B, N = 32, 128256
+    xt = torch.randn(B, N, generator=torch.Generator().manual_seed(0))
+    x = xt.numpy()
+    nbytes = B * N * 4 + B * 4
+    allt = O.host_threads()
+    saved = torch.get_num_threads()
+    out = {"config": f"({B},{N}) fp32 x~N(0,1) seed 0", "host_threads": allt, "cpu": _cpu_name(),
+           "reps": reps}
+
+    def med(fn):
+        fn()
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        ms = statistics.median(ts) * 1e3
+        return {"ms": ms, "GB_s": nbytes / (ms * 1e-3) / 1e9}
+
+    try:
+        if O.ref_available("simd"):
+            out["intlse_avx2_1t"] = med(lambda: O.ref_simd_rows(x, threads=1))
+            out["intlse_avx2_all"] = med(lambda: O.ref_simd_rows(x, threads=allt))
+        if O.ref_available("ref_fused_cpu"):
+            m = O.ref_ext("ref_fused_cpu")
+            torch.set_num_threads(1)
+            out["fuselse_cpu_1t"] = med(lambda: m.cpu_lse_float(xt))
+            torch.set_num_threads(allt)
+            out["fuselse_cpu_all"] = med(lambda: m.cpu_lse_float(xt))
+        torch.set_num_threads(1)
+        out["torch_logsumexp_1t"] = med(lambda: torch.logsumexp(xt, -1))
+        torch.set_num_threads(allt)
+        out["torch_logsumexp_all"] = med(lambda: torch.logsumexp(xt, -1))
+    finally:
+        torch.set_num_threads(saved)
+    return out
+
+
 def _cpu_name():
     try:
         for line in Path("/proc/cpuinfo").read_text().splitlines():
@@ -604,7 +859,14 @@ def main():
     ap.add_argument("--workload", default="fwdbwd_f32")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the `strong` and `vocab_exchange` measurements")
     ap.add_argument("--flush-l2", action="store_true", help="evict L2 between timed steps")
+    ap.add_argument("--kernel-graphs", action="store_true",
+                    help="report the step as the sum of the per-kernel pass (a graph per kernel, "
+                         "events between kernels) instead of the step pass (one graph per step)")
+    ap.add_argument("--same-input", action="store_true",
+                    help="fwd/bwd workloads: one input batch every step instead of two alternating")
     ap.add_argument("--eager", action="store_true",
                     help="launch the timed kernels eagerly instead of from CUDA graphs")
     args = ap.parse_args()
@@ -624,12 +886,19 @@ def main():
         from datetime import timedelta
         torch.distributed.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
 
-    wl = make_workload(args.workload, dev, seed=rank, world=world, rank=rank)
+    wl = make_workload(args.workload, dev, seed=rank, world=world, rank=rank,
+                       same_input=args.same_input)
     with ClockSampler(local) as clk:
+        # per-kernel pass: a graph per kernel, CUDA events between kernels
         step_ms, per_kernel = run_timed(wl, args.steps, args.warmup, dev, dist_on, args.flush_l2,
                                         graphs=not args.eager)
+        kernel_pass_ms = step_ms
+        step_graph = not (args.eager or args.kernel_graphs)
+        if step_graph:  # step pass: one graph per step, events at step boundaries
+            step_ms = run_step_graphs(wl, args.steps, args.warmup, dev, dist_on, args.flush_l2)
     clocks = clk.summary()
     step_ms = max_over_ranks(step_ms, dist_on, dev)
+    kernel_pass_ms = max_over_ranks(kernel_pass_ms, dist_on, dev)
     per_kernel = [max_over_ranks(v, dist_on, dev) for v in per_kernel]
     ks = wl.kernels()
     bytes_step = sum(b for _, _, b in ks)
@@ -647,6 +916,12 @@ def main():
                    "frac_of_peak": b / (t * 1e-3) / 1e9 / peaks["hbm_gbs"]}
                for (l, _, b), t in zip(ks, per_kernel)}
 
+    extra = {}
+    if args.workload == "fwdbwd_f32" and not args.no_extra:
+        extra["strong"] = strong_record(dev, world, rank, args.steps, args.warmup, dist_on, step_ms)
+        extra["vocab_exchange"] = vocab_exchange_record(dev, world, rank, args.steps, args.warmup,
+                                                        dist_on)
+
     e2e = None
     if not args.no_e2e and hasattr(wl, "e2e_step"):
         e2e_ms = max_over_ranks(run_e2e(wl, max(3, args.steps // 4), 3, dev, dist_on), dist_on, dev)
@@ -660,6 +935,10 @@ def main():
             cpu = cpu_baseline(rows=B_ROWS)
         except Exception as exc:  # the baseline is reported, never required
             cpu = {"value": None, "error": repr(exc)}
+        try:
+            cpu["reference_cpu_configs"] = cpu_reference_configs()
+        except Exception as exc:
+            cpu["reference_cpu_configs"] = {"error": repr(exc)}
 
     if rank == 0:
         line = {"metric": METRIC if args.workload == "fwdbwd_f32" else f"{wl.name} HBM GB/s",
@@ -667,13 +946,16 @@ def main():
                 "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
                 "config": dict(wl.config, parallelism=f"rows x{world}" if world > 1 else "1 GPU",
-                               launch="eager" if args.eager else "CUDA graph per kernel",
+                               launch=("eager" if args.eager else
+                                       "one CUDA graph per step (all its kernels), events at step "
+                                       "boundaries" if step_graph else "CUDA graph per kernel"),
                                l2_flush=bool(args.flush_l2)),
+                "ms_per_step_kernel_pass": kernel_pass_ms,
                 "rows_per_s": world * wl.rows() / (step_ms * 1e-3),
                 "pct_of_peak": 100.0 * value / (world * peaks["hbm_gbs"]),
                 "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu, "e2e": e2e,
                 "clocks": clocks, "gpu_launches": wl.launches_per_step * args.steps,
-                "gpu": torch.cuda.get_device_name(dev)}
+                "gpu": torch.cuda.get_device_name(dev), **extra}
         print(json.dumps(line), flush=True)
     if dist_on:
         torch.distributed.barrier()
