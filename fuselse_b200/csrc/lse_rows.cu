@@ -25,7 +25,6 @@
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
 #include <algorithm>
-#include <atomic>
 #include <cstdlib>
 
 namespace cg = cooperative_groups;
@@ -126,128 +125,6 @@ __global__ void __launch_bounds__(FwdShape<T>::kThreads) lse_segment_kernel(
         }
     }
     if (threadIdx.x == 0 && row < B) write_row<T, MODE>(out, row, m, s, empty_value, tg, sel);
-}
-
-// Long dense rows staged through shared memory: one CTA per row, its thread 0
-// streaming the row's 16-byte-aligned body into a ring of kBulkStages buffers
-// of 16 KB with 1-D bulk copies (cp.async.bulk, completion counted in bytes on
-// one mbarrier per buffer), all threads folding each buffer from shared
-// memory and releasing it through a second mbarrier (one arrival per warp)
-// before thread 0 refills it.  The bytes in flight per CTA are the ring, not
-// the loads a thread can hold in registers.  Head and tail elements (before
-// the first / after the last 16-byte boundary) are read directly.  Every wait
-// is bounded (~1 s): a row whose copies never complete gives NaN and bumps
-// *err_count, after thread 0 has waited (bounded) for the copies it issued.
-#ifndef FL_FWD_BULK
-#define FL_FWD_BULK 0
-#endif
-#ifndef FL_BULK_STAGES
-#define FL_BULK_STAGES 3
-#endif
-constexpr int kBulkThreads = 256;
-constexpr int kBulkStages = FL_BULK_STAGES;
-constexpr int kBulkStageBytes = 16384;
-constexpr int kBulkStageVecs = kBulkStageBytes / 16;
-constexpr int kBulkVecsPerThread = kBulkStageVecs / kBulkThreads;  // 4
-constexpr int kBulkSmem = kBulkStages * kBulkStageBytes;
-
-__device__ int g_bulk_wait_errors;  // rows given up on (copies never completed)
-
-template <typename T, int MODE>
-__global__ void __launch_bounds__(kBulkThreads, 4) lse_bulk_kernel(
-    const T* __restrict__ x, float* __restrict__ out, int64_t B, int64_t N,
-    float empty_value, SelArgs sel, RowMap rm) {
-    constexpr int E = Elem<T>::kPerVec;
-    extern __shared__ __align__(128) unsigned char ring[];
-    __shared__ uint64_t full[kBulkStages], empty[kBulkStages];
-    const int64_t row = blockIdx.x;
-    const int lane = threadIdx.x & 31;
-    const T* rowp = x + rm(row);
-    const int64_t head = head_elems(rowp, N);
-    const int64_t nv = (N - head) / E;
-    const int64_t tail0 = head + nv * E;
-    const unsigned char* body = reinterpret_cast<const unsigned char*>(rowp + head);
-    const int64_t nstage = (nv + kBulkStageVecs - 1) / kBulkStageVecs;
-
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < kBulkStages; ++i) {
-            mbar_init(&full[i], 1);
-            mbar_init(&empty[i], kBulkThreads / 32);
-        }
-        mbar_init_fence();
-    }
-    __syncthreads();
-    pdl_wait();
-    pdl_launch_dependents();
-    int64_t issued = 0;  // thread 0 only
-    auto issue = [&](int64_t k) {
-        const int slot = static_cast<int>(k % kBulkStages);
-        const int64_t v0 = k * kBulkStageVecs;
-        const uint32_t bytes = static_cast<uint32_t>(min(nv - v0, (int64_t)kBulkStageVecs) * 16);
-        mbar_arrive_expect_tx(&full[slot], bytes);
-        bulk_load(ring + slot * kBulkStageBytes, body + v0 * 16, bytes, &full[slot]);
-        issued = k + 1;
-    };
-    if (threadIdx.x == 0)
-        for (int64_t k = 0; k < nstage && k < kBulkStages; ++k) issue(k);
-
-    Target<T> tg;
-    if (MODE == kOutSelect && threadIdx.x == 0) tg.fetch(rowp, N, row, sel);
-    float m = -INFINITY, s = 0.0f;
-    // head / tail elements overlap the first copies
-    if (threadIdx.x < head) ms_fold1(m, s, Elem<T>::load1(rowp + threadIdx.x));
-    if (tail0 + threadIdx.x < N) ms_fold1(m, s, Elem<T>::load1(rowp + tail0 + threadIdx.x));
-
-    bool ok = true;
-    int64_t k = 0;
-    for (; k < nstage; ++k) {
-        const int slot = static_cast<int>(k % kBulkStages);
-        const uint32_t parity = static_cast<uint32_t>((k / kBulkStages) & 1);
-        if (!mbar_wait_bounded(&full[slot], parity)) {
-            ok = false;
-            break;
-        }
-        const uint4* sv = reinterpret_cast<const uint4*>(ring + slot * kBulkStageBytes);
-        const int64_t left = nv - k * kBulkStageVecs;
-        if (left >= kBulkStageVecs) {
-            float v[kBulkVecsPerThread * E];
-#pragma unroll
-            for (int u = 0; u < kBulkVecsPerThread; ++u)
-                Elem<T>::unpack(sv[threadIdx.x + u * kBulkThreads], v + u * E);
-            ms_fold<kBulkVecsPerThread * E, FwdShape<T>::kPoly>(m, s, v);
-        } else {
-            for (int i = threadIdx.x; i < left; i += kBulkThreads) {
-                float v[E];
-                Elem<T>::unpack(sv[i], v);
-                ms_fold<E, FwdShape<T>::kPoly>(m, s, v);
-            }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
-        if (threadIdx.x == 0 && k + kBulkStages < nstage) {
-            if (!mbar_wait_bounded(&empty[slot], parity)) {
-                ok = false;
-                break;
-            }
-            issue(k + kBulkStages);
-        }
-    }
-    if (!ok && threadIdx.x == 0) {
-        // do not leave the CTA while a copy it issued may still land in its
-        // shared memory: wait (bounded) for every issued stage not yet consumed
-        for (int64_t j = k; j < issued; ++j)
-            mbar_wait_bounded(&full[j % kBulkStages], static_cast<uint32_t>((j / kBulkStages) & 1));
-        atomicAdd(&g_bulk_wait_errors, 1);
-    }
-    const int bad = __syncthreads_or(!ok);
-    ms_block_reduce<kBulkThreads>(m, s);
-    if (threadIdx.x == 0) {
-        if (bad) {
-            m = __int_as_float(0x7fc00000);
-            s = 0.0f;
-        }
-        write_row<T, MODE>(out, row, m, s, empty_value, tg, sel);
-    }
 }
 
 // One warp per row for short rows.
@@ -449,21 +326,6 @@ int launch_rows(const T* x, float* out, int64_t B, int64_t N, float empty_value,
         return check_launch(what);
     }
     const int nseg = choose_nseg<T>(B, N);
-    if (FL_FWD_BULK && nseg == 1 && N * (int64_t)sizeof(T) >= 4 * kBulkStageBytes) {
-        static std::atomic<uint64_t> configured{0};  // one bit per device
-        int dev = 0;
-        FL_CUDA(cudaGetDevice(&dev));
-        const uint64_t bit = 1ull << (dev & 63);
-        if (!(configured.load(std::memory_order_relaxed) & bit)) {
-            FL_CUDA(cudaFuncSetAttribute(lse_bulk_kernel<T, MODE>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kBulkSmem));
-            configured.fetch_or(bit, std::memory_order_relaxed);
-        }
-        FL_REQUIRE(B <= INT32_MAX, "%s: B=%lld too large", what, (long long)B);
-        LaunchCfg lc(dim3((unsigned)B), dim3(kBulkThreads), kBulkSmem, stream);
-        FL_CUDA(cudaLaunchKernelEx(&lc.cfg, lse_bulk_kernel<T, MODE>, x, out, B, N, empty_value, sel, rm));
-        return check_launch(what);
-    }
     const int64_t grid = B * nseg;
     FL_REQUIRE(grid <= INT32_MAX, "%s: B=%lld too large", what, (long long)B);
     LaunchCfg lc(dim3((unsigned)grid), dim3(FwdShape<T>::kThreads), 0, stream);
