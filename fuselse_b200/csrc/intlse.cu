@@ -57,6 +57,10 @@ enum Kind { kQ16F32 = 0, kQ16I32 = 1, kQ106I16 = 2 };
 #ifndef FL_INTLSE_PERSIST_ROW_BYTES
 #define FL_INTLSE_PERSIST_ROW_BYTES 4096
 #endif
+// Aligned rows of 1024*K elements (K <= 8) take intlse_whole_rounds_kernel.
+#ifndef FL_INTLSE_WHOLE_ROUNDS
+#define FL_INTLSE_WHOLE_ROUNDS 1
+#endif
 
 // Reference constants (lse_kernel.cu:23-27): CONV = LOG2_E * 2^16 and
 // LN_2 / 2^16 from the same decimal literals, so the float values match.
@@ -258,6 +262,68 @@ __global__ void __launch_bounds__(CTA) intlse_rows_kernel(
     }
 }
 
+// Rows made of whole rounds only — every row starts on a vector boundary (no
+// head elements), N = 1024*K (no partial round, no tail), K <= 8 — one CTA per
+// row.  Each chain loads its K vectors at once; the correction table is filled
+// while they are in flight, so the table's barrier costs no extra latency; the
+// K*4 pair steps then run with no per-round predicates or address updates.
+// The order is intlse_rows_kernel's exactly: element 0 of vector t seeds chain
+// t, then the rest of vector t, then vectors t+256, t+512, ..., then the two
+// butterflies.
+template <int KIND, bool LUT, int K>
+__global__ void __launch_bounds__(256) intlse_whole_rounds_kernel(
+    const typename IK<KIND>::In* __restrict__ x, float* __restrict__ out, int64_t N) {
+    constexpr int F = IK<KIND>::F;
+    __shared__ __align__(16) int lut_s[64 * 32];
+    __shared__ int warp_val[8];
+    const int t = threadIdx.x;
+    const int lane = t & 31;
+    const int64_t row = blockIdx.x;
+    const typename IK<KIND>::In* vp = x + row * N + 4 * t;
+    Q4 q[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) q[k] = load_vec_at<KIND>(vp + k * 1024);
+    if constexpr (LUT) fill_lane_lut<256>(lut_s, F == 16 ? kLutQ16 : kLutQ10_6);
+    __syncthreads();
+    const LaneLut lut{lut_s, lane};
+    int acc = q[0].v[0];
+#pragma unroll
+    for (int e = 1; e < 4; ++e) acc = pair_exact<F, LUT>(acc, q[0].v[e], lut);
+#pragma unroll
+    for (int k = 1; k < K; ++k)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc = pair_exact<F, LUT>(acc, q[k].v[e], lut);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+        acc = pair_exact<F, LUT>(acc, __shfl_xor_sync(0xffffffffu, acc, off), lut);
+    if (lane == 0) warp_val[t >> 5] = acc;
+    __syncthreads();
+    if (t < 32) {
+        int v = lane < 8 ? warp_val[lane] : kQNegInf;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1)
+            v = pair_exact<F, LUT>(v, __shfl_xor_sync(0xffffffffu, v, off), lut);
+        if (lane == 0) out[row] = to_output<F>(v);
+    }
+}
+
+template <int KIND, bool LUT>
+int launch_whole_rounds(const typename IK<KIND>::In* x, float* out, int64_t B, int64_t N,
+                        cudaStream_t stream) {
+    const unsigned grid = static_cast<unsigned>(B);
+    switch (N / 1024) {
+        case 1: intlse_whole_rounds_kernel<KIND, LUT, 1><<<grid, 256, 0, stream>>>(x, out, N); break;
+        case 2: intlse_whole_rounds_kernel<KIND, LUT, 2><<<grid, 256, 0, stream>>>(x, out, N); break;
+        case 3: intlse_whole_rounds_kernel<KIND, LUT, 3><<<grid, 256, 0, stream>>>(x, out, N); break;
+        case 4: intlse_whole_rounds_kernel<KIND, LUT, 4><<<grid, 256, 0, stream>>>(x, out, N); break;
+        case 5: intlse_whole_rounds_kernel<KIND, LUT, 5><<<grid, 256, 0, stream>>>(x, out, N); break;
+        case 6: intlse_whole_rounds_kernel<KIND, LUT, 6><<<grid, 256, 0, stream>>>(x, out, N); break;
+        case 7: intlse_whole_rounds_kernel<KIND, LUT, 7><<<grid, 256, 0, stream>>>(x, out, N); break;
+        default: intlse_whole_rounds_kernel<KIND, LUT, 8><<<grid, 256, 0, stream>>>(x, out, N); break;
+    }
+    return FL_OK;
+}
+
 template <int KIND, bool LUT, int CTA, int D>
 int launch_cfg(const typename IK<KIND>::In* x, float* out, int64_t B, int64_t N,
                cudaStream_t stream) {
@@ -312,7 +378,14 @@ int launch_intlse(const typename IK<KIND>::In* x, float* out, int64_t B, int64_t
     const int64_t K = (N / 4 + 255) / 256;  // rounds per row
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     int st;
-    if (B * 256 >= FL_INTLSE_FILL_WARPS * 32 * sms) {
+    const bool whole_rounds = FL_INTLSE_WHOLE_ROUNDS && aligned_to(x, IK<KIND>::VB) &&
+                              (N * (int64_t)sizeof(In)) % IK<KIND>::VB == 0 && N % 1024 == 0 &&
+                              N >= 1024 && N <= 8 * 1024 &&
+                              N * (int64_t)sizeof(In) > FL_INTLSE_PERSIST_ROW_BYTES &&
+                              B <= INT32_MAX;
+    if (B * 256 >= FL_INTLSE_FILL_WARPS * 32 * sms && whole_rounds) {
+        st = launch_whole_rounds<KIND, LUT>(x, out, B, N, s);
+    } else if (B * 256 >= FL_INTLSE_FILL_WARPS * 32 * sms) {
         // chains enough to give every SM FL_INTLSE_FILL_WARPS warps: one
         // 256-thread CTA per row, few rounds in flight (registers for occupancy)
         st = K > 8 ? launch_d<KIND, LUT, FL_INTLSE_DMID>(x, out, B, N, 1, s)

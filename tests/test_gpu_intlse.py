@@ -162,3 +162,24 @@ def test_many_short_rows_all_kinds(ext, B, N, phase):
     qs = _phased(torch.clamp(torch.round(x * 64), -32768, 32767).to(torch.int16), phase)
     want, _ = O.intlse_rows(qs.cpu().numpy(), O.Q10_6_I16, True, base_phase=(phase * 2) % 16)
     np.testing.assert_array_equal(_bits(ext.batched_logsumexp_q10_6(qs)), want.view(np.int32))
+
+
+@pytest.mark.parametrize("N", [2048, 3072, 4096, 5120, 7168, 8192])
+@pytest.mark.parametrize("phase", [0, 1])
+def test_whole_round_rows_all_kinds(ext, N, phase):
+    """Rows of 1024*K elements, plentiful: aligned (phase 0) they take the
+    whole-rounds kernel (all of a chain's vectors loaded at once, no per-round
+    predicates), misaligned (phase 1) the general one — bit for bit either way,
+    with and without the correction table."""
+    B = 600
+    x = _phased(_x(B, N, seed=N + phase, scale=3.0), phase)
+    want, _ = O.intlse_rows(x.cpu().numpy(), O.Q16_F32, True, base_phase=(phase * 4) % 16)
+    np.testing.assert_array_equal(_bits(ext.batched_logsumexp(x)), want.view(np.int32))
+    want, _ = O.intlse_rows(x.cpu().numpy(), O.Q16_F32, False, base_phase=(phase * 4) % 16)
+    np.testing.assert_array_equal(_bits(ext.batched_logsumexp_nolut(x)), want.view(np.int32))
+    qi = _phased(torch.from_numpy(_q16_from_f32(x.cpu().numpy())).cuda(), phase)
+    want, _ = O.intlse_rows(qi.cpu().numpy(), O.Q16_I32, True, base_phase=(phase * 4) % 16)
+    np.testing.assert_array_equal(_bits(ext.batched_logsumexp_q16_i32(qi)), want.view(np.int32))
+    qs = _phased(torch.clamp(torch.round(x * 64), -32768, 32767).to(torch.int16), phase)
+    want, _ = O.intlse_rows(qs.cpu().numpy(), O.Q10_6_I16, True, base_phase=(phase * 2) % 16)
+    np.testing.assert_array_equal(_bits(ext.batched_logsumexp_q10_6(qs)), want.view(np.int32))
