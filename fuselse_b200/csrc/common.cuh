@@ -51,6 +51,38 @@ int check_launch(const char* what);
         }                                                                    \
     } while (0)
 
+// Launch configuration with programmatic stream serialization
+// (the kernel may be scheduled while its predecessor in the stream drains;
+// it orders itself with pdl_wait before touching memory), plus an optional
+// cluster shape.
+#ifndef FL_PDL
+#define FL_PDL 1
+#endif
+struct LaunchCfg {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[2];
+    LaunchCfg(dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl = FL_PDL) {
+        cfg.gridDim = grid;
+        cfg.blockDim = block;
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = stream;
+        cfg.attrs = attr;
+        cfg.numAttrs = 0;
+        if (pdl) {
+            attr[cfg.numAttrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[cfg.numAttrs].val.programmaticStreamSerializationAllowed = 1;
+            ++cfg.numAttrs;
+        }
+    }
+    void cluster(int n) {
+        attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
+        attr[cfg.numAttrs].val.clusterDim.x = n;
+        attr[cfg.numAttrs].val.clusterDim.y = 1;
+        attr[cfg.numAttrs].val.clusterDim.z = 1;
+        ++cfg.numAttrs;
+    }
+};
+
 // Resident CTAs per SM of `kernel` at `threads` per CTA (at least 1), cached in
 // `slot` (0 = not yet known; concurrent first calls store the same value).
 template <typename Kernel>

@@ -248,38 +248,6 @@ __global__ void __launch_bounds__(kThreads) lse_bwd_kernel(
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-// Launch configuration of the row kernels: programmatic stream serialization
-// (the kernel may be scheduled while its predecessor in the stream drains;
-// it orders itself with pdl_wait before touching memory), plus an optional
-// cluster shape.
-#ifndef FL_PDL
-#define FL_PDL 1
-#endif
-struct LaunchCfg {
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[2];
-    LaunchCfg(dim3 grid, dim3 block, size_t smem, cudaStream_t stream) {
-        cfg.gridDim = grid;
-        cfg.blockDim = block;
-        cfg.dynamicSmemBytes = smem;
-        cfg.stream = stream;
-        cfg.attrs = attr;
-        cfg.numAttrs = 0;
-        if (FL_PDL) {
-            attr[cfg.numAttrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-            attr[cfg.numAttrs].val.programmaticStreamSerializationAllowed = 1;
-            ++cfg.numAttrs;
-        }
-    }
-    void cluster(int n) {
-        attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
-        attr[cfg.numAttrs].val.clusterDim.x = n;
-        attr[cfg.numAttrs].val.clusterDim.y = 1;
-        attr[cfg.numAttrs].val.clusterDim.z = 1;
-        ++cfg.numAttrs;
-    }
-};
-
 int env_int(const char* name, int dflt) {
     const char* v = std::getenv(name);
     if (!v || !*v) return dflt;
@@ -403,8 +371,10 @@ extern "C" int fl_lse_combine(const float* ms, float* out, int64_t G, int64_t B,
     if (int st = bind_device(stream, out)) return st;
     const int64_t grid = (B + 255) / 256;
     FL_REQUIRE(grid <= INT32_MAX, "fl_lse_combine: B too large");
-    lse_combine_kernel<<<(unsigned)grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        reinterpret_cast<const float2*>(ms), out, G, B);
+    LaunchCfg lc(dim3((unsigned)grid), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
+                 /*pdl=*/false);
+    FL_CUDA(cudaLaunchKernelEx(&lc.cfg, lse_combine_kernel, reinterpret_cast<const float2*>(ms), out,
+                               G, B));
     return check_launch("fl_lse_combine");
 }
 
