@@ -712,6 +712,43 @@ def run_e2e(wl, steps, warmup, dev, dist_on):
     return s.elapsed_time(e) / steps
 
 
+def copy_floor(wl, steps, dev, dist_on):
+    """The e2e step's host-link floor: the same bytes copied alone — the step's
+    input from pinned host memory to the device on one stream while a device
+    buffer of the output's size goes back to pinned host memory on another,
+    every rank at once (the GPUs share the host's memory and PCIe root) — no
+    kernel.  Returns ms per step."""
+    dst = torch.empty_like(wl.x)
+    up, down = torch.cuda.Stream(), torch.cuda.Stream()
+    cur = torch.cuda.current_stream()
+
+    def once():
+        up.wait_stream(cur)
+        down.wait_stream(cur)
+        with torch.cuda.stream(up):
+            dst.copy_(wl.x_host, non_blocking=True)
+        with torch.cuda.stream(down):
+            wl.gx_host.copy_(wl.x, non_blocking=True)
+        cur.wait_stream(up)
+        cur.wait_stream(down)
+
+    once()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist_on:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(steps):
+        once()
+    e.record()
+    torch.cuda.synchronize()
+    if dist_on:
+        torch.distributed.barrier()
+    del dst
+    return s.elapsed_time(e) / steps
+
+
 def max_over_ranks(v, dist_on, dev):
     if not dist_on:
         return v
@@ -925,9 +962,15 @@ def main():
     e2e = None
     if not args.no_e2e and hasattr(wl, "e2e_step"):
         e2e_ms = max_over_ranks(run_e2e(wl, max(3, args.steps // 4), 3, dev, dist_on), dist_on, dev)
+        floor_ms = max_over_ranks(copy_floor(wl, 3, dev, dist_on), dist_on, dev)
         e2e = {"value": world * bytes_step / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
                "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h, "ms_per_step": e2e_ms,
-               "api": getattr(wl, "e2e_api", "public API")}
+               "api": getattr(wl, "e2e_api", "public API"),
+               "copy_floor_ms": floor_ms,
+               "copy_floor_value": world * bytes_step / (floor_ms * 1e-3) / 1e9,
+               "copy_floor": "the step's input uploaded and a buffer of its output's size downloaded, "
+                             "pinned host memory, concurrently on two streams, no kernel, all ranks "
+                             "at once: the host link's bound on e2e"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "fwdbwd_f32":
