@@ -146,9 +146,7 @@ __global__ void __launch_bounds__(kCombineThreads) vocab_combine_kernel(
 }
 
 // The scatter and combine kernels of one exchange call on `s`, in plain stream
-// order (launching the combine early with programmatic serialization measured
-// 10 us slower per (8192, 16032) fp16 call: its CTAs waited on SMs the
-// scatter's last wave needed).
+// order.
 int launch_exchange(const void* x, int dtype, int64_t B, int64_t N, unsigned char* const* peers,
                     unsigned char* local, int rank, int G, float* out, uint64_t wait_ns,
                     cudaStream_t s, const char* what) {
