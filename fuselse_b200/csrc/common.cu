@@ -25,22 +25,41 @@ void clear_error() { g_last_error.clear(); }
 static thread_local fl_stream_t t_last_stream = nullptr;
 static thread_local int t_last_dev = -1;
 
+// Device of a device (or managed) pointer.
+static int pointer_device(const void* ptr, int* dev) {
+    cudaPointerAttributes attr;
+    FL_CUDA(cudaPointerGetAttributes(&attr, ptr));
+    if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged) {
+        set_error("pointer %p is not device memory", ptr);
+        return FL_ERR_INVALID_ARGUMENT;
+    }
+    *dev = attr.device;
+    return FL_OK;
+}
+
 int bind_device(fl_stream_t stream, const void* ptr) {
     int dev = -1;
     if (stream != nullptr && stream == t_last_stream) {
         dev = t_last_dev;
     } else if (stream != nullptr) {
-        FL_CUDA(cudaStreamGetDevice(reinterpret_cast<cudaStream_t>(stream), &dev));
+        // A stream being captured into a CUDA graph refuses cudaStreamGetDevice,
+        // and the refusal invalidates the capture; cudaStreamIsCapturing is
+        // allowed.  While capturing, the device is the one of the output
+        // buffer (every entry point passes one).
+        const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        FL_CUDA(cudaStreamIsCapturing(s, &cs));
+        if (cs == cudaStreamCaptureStatusNone) {
+            FL_CUDA(cudaStreamGetDevice(s, &dev));
+        } else if (ptr != nullptr) {
+            if (int st = pointer_device(ptr, &dev)) return st;
+        } else {
+            FL_CUDA(cudaGetDevice(&dev));
+        }
         t_last_stream = stream;
         t_last_dev = dev;
     } else if (ptr != nullptr) {
-        cudaPointerAttributes attr;
-        FL_CUDA(cudaPointerGetAttributes(&attr, ptr));
-        if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged) {
-            set_error("pointer %p is not device memory", ptr);
-            return FL_ERR_INVALID_ARGUMENT;
-        }
-        dev = attr.device;
+        if (int st = pointer_device(ptr, &dev)) return st;
     } else {
         FL_CUDA(cudaGetDevice(&dev));
     }
