@@ -32,7 +32,7 @@ Barrier and synchronize around each timed region; max over ranks.
 
 `e2e` (default workload): the same metric through the public host-buffer API
 (fuselse_b200.host.HostRowPipeline): every step x and g are copied in from
-pinned host memory and lse and the gradient copied back, in 64-row chunks
+pinned host memory and lse and the gradient copied back, in ~16 MB chunks
 whose uploads, kernels and downloads overlap on three streams; h2d/d2h bytes
 are those copies.
 
@@ -207,14 +207,15 @@ class FwdBwdF32(Workload):
     # kernels chunk by chunk (fuselse_b200.host.HostRowPipeline)
     def e2e_setup(self, dev):
         from fuselse_b200.host import HostRowPipeline
-        self.pipe = HostRowPipeline(self.N, device=dev, chunk_rows=64, depth=3, robust=True)
+        self.pipe = HostRowPipeline(self.N, device=dev, depth=3, robust=True)
         self.x_host = self.x.cpu().pin_memory()
         self.g_host = self.g.cpu().pin_memory()
         self.gx_host = torch.empty_like(self.x_host).pin_memory()
         self.lse_host = torch.empty(self.B).pin_memory()
         self.h2d = self.x_host.numel() * 4 + self.g_host.numel() * 4
         self.d2h = self.gx_host.numel() * 4 + self.lse_host.numel() * 4
-        self.e2e_api = "fuselse_b200.host.HostRowPipeline.run (64-row chunks, copies overlapped)"
+        self.e2e_api = (f"fuselse_b200.host.HostRowPipeline.run ({self.pipe.rows}-row chunks, "
+                        "copies overlapped)")
 
     def e2e_step(self, dev):
         self.pipe.run(self.x_host, self.lse_host, self.g_host, self.gx_host)
