@@ -110,3 +110,24 @@ def test_sparse_bwd_workspace_checks_without_gpu():
                              70, 1, ctypes.c_void_p(4096), 1024, None, None)
     assert st == _lib.FL_ERR_INVALID_ARGUMENT
     assert b"workspace" in L.fl_last_error()
+
+
+def test_ipc_and_query_arguments_checked_without_gpu():
+    """The exchange-buffer helpers and the binary-version query reject bad
+    arguments before any CUDA call."""
+    from fuselse_b200 import _lib
+    L = _lib.lib()
+    ptr = ctypes.c_void_p()
+    handle = (ctypes.c_ubyte * 64)()
+    assert L.fl_ipc_buffer_alloc(-1, 1024, ctypes.byref(ptr), handle) == _lib.FL_ERR_INVALID_ARGUMENT
+    assert L.fl_ipc_buffer_alloc(0, 0, ctypes.byref(ptr), handle) == _lib.FL_ERR_INVALID_ARGUMENT
+    assert L.fl_ipc_buffer_alloc(0, 1 << 41, ctypes.byref(ptr), handle) == _lib.FL_ERR_INVALID_ARGUMENT
+    assert L.fl_ipc_buffer_alloc(0, 1024, None, handle) == _lib.FL_ERR_INVALID_ARGUMENT
+    assert L.fl_ipc_buffer_open(0, None, ctypes.byref(ptr)) == _lib.FL_ERR_INVALID_ARGUMENT
+    assert L.fl_ipc_buffer_open(-2, handle, ctypes.byref(ptr)) == _lib.FL_ERR_INVALID_ARGUMENT
+    assert L.fl_ipc_buffer_close(0, None) == _lib.FL_ERR_INVALID_ARGUMENT
+    assert L.fl_ipc_buffer_free(-1, None) == _lib.FL_ERR_INVALID_ARGUMENT
+    assert L.fl_ipc_buffer_free(0, None) == _lib.FL_OK  # freeing nothing is a no-op
+    v = ctypes.c_int()
+    assert L.fl_binary_version(-1, ctypes.byref(v)) == _lib.FL_ERR_INVALID_ARGUMENT
+    assert L.fl_binary_version(0, None) == _lib.FL_ERR_INVALID_ARGUMENT
