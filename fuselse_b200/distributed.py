@@ -230,6 +230,8 @@ class VocabShardExchange:
         import ctypes
 
         from . import _lib
+        if getattr(self, "buf", None) is None:
+            raise RuntimeError("this exchange was closed")
         if x_shard.dim() != 2 or x_shard.size(0) != self.rows:
             raise RuntimeError(f"expected a ({self.rows}, N) shard, got {tuple(x_shard.shape)}")
         if not (x_shard.is_cuda and x_shard.device == self.device and x_shard.is_contiguous()):
@@ -246,6 +248,8 @@ class VocabShardExchange:
 
     def error(self) -> bool:
         """True once a combine gave up waiting for a peer (sticky)."""
+        if getattr(self, "buf", None) is None:
+            raise RuntimeError("this exchange was closed")
         return bool(self.buf[4:8].view(torch.int32).item())
 
 

@@ -254,3 +254,12 @@ def test_state_does_not_drift_over_many_merges(ext):
     lse = ext.onepass_lse_float_robust(x).cpu().numpy().astype(np.float64)
     want = O.lse_f64(x.cpu().numpy())
     assert np.abs(lse - want).max() <= 8 * np.spacing(np.float32(40.0 + np.log(N)))
+
+
+def test_vocab_exchange_single_rank_close(ext):
+    from fuselse_b200.distributed import VocabShardExchange
+    ex = VocabShardExchange.single_rank(8)
+    x = _randn(8, 100, seed=1)
+    _close(ex(x).cpu().numpy(), O.lse_f64(x.cpu().numpy()), RTOL32)
+    ex.close()  # a single-rank exchange owns a torch buffer: nothing to unmap
+    assert not ex.error()
