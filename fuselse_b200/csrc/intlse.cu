@@ -105,27 +105,70 @@ struct Q4 {
     int v[4];
 };
 
+// A vector as loaded (16 bytes for Q16.16 input, 8 for Q10.6).  Kept raw in
+// the round buffers of the scarce-row shape and widened only when its round is
+// paired: a warp issues in order, so widening right after the load stalls it on
+// that load, and there are too few warps to hide it.
 template <int KIND>
-__device__ __forceinline__ Q4 load_vec_at(const typename IK<KIND>::In* v) {
-    Q4 q;
+struct RawVec {
+    uint4 r;
+};
+template <>
+struct RawVec<kQ106I16> {
+    uint2 r;
+};
+
+template <int KIND>
+__device__ __forceinline__ RawVec<KIND> load_raw(const typename IK<KIND>::In* v) {
+    RawVec<KIND> q;
     if constexpr (KIND == kQ106I16) {
-        uint32_t a, b;
         asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
-                     : "=r"(a), "=r"(b)
+                     : "=r"(q.r.x), "=r"(q.r.y)
                      : "l"(v));
-        q.v[0] = (int)(int16_t)(a & 0xffffu);
-        q.v[1] = (int)a >> 16;
-        q.v[2] = (int)(int16_t)(b & 0xffffu);
-        q.v[3] = (int)b >> 16;
     } else {
-        const uint4 r = ld_stream_u4(v);
-        q.v[0] = IK<KIND>::conv(r.x);
-        q.v[1] = IK<KIND>::conv(r.y);
-        q.v[2] = IK<KIND>::conv(r.z);
-        q.v[3] = IK<KIND>::conv(r.w);
+        q.r = ld_stream_u4(v);
     }
     return q;
 }
+
+template <int KIND>
+__device__ __forceinline__ Q4 widen(const RawVec<KIND>& raw) {
+    Q4 q;
+    if constexpr (KIND == kQ106I16) {
+        q.v[0] = (int)(int16_t)(raw.r.x & 0xffffu);
+        q.v[1] = (int)raw.r.x >> 16;
+        q.v[2] = (int)(int16_t)(raw.r.y & 0xffffu);
+        q.v[3] = (int)raw.r.y >> 16;
+    } else {
+        q.v[0] = IK<KIND>::conv(raw.r.x);
+        q.v[1] = IK<KIND>::conv(raw.r.y);
+        q.v[2] = IK<KIND>::conv(raw.r.z);
+        q.v[3] = IK<KIND>::conv(raw.r.w);
+    }
+    return q;
+}
+
+template <int KIND>
+__device__ __forceinline__ Q4 load_vec_at(const typename IK<KIND>::In* v) {
+    return widen<KIND>(load_raw<KIND>(v));
+}
+
+// Round-buffer entry: raw when RAW (many rounds in flight, few warps: the
+// scarce-row shape measured 190 -> 156 us for fp32 input at (64, 1048576)),
+// else widened at load (4 rounds in flight at full occupancy, where widening
+// at use measured no better).
+template <int KIND, bool RAW>
+struct RoundBuf {
+    RawVec<KIND> raw;
+    __device__ __forceinline__ void load(const typename IK<KIND>::In* v) { raw = load_raw<KIND>(v); }
+    __device__ __forceinline__ Q4 get() const { return widen<KIND>(raw); }
+};
+template <int KIND>
+struct RoundBuf<KIND, false> {
+    Q4 q;
+    __device__ __forceinline__ void load(const typename IK<KIND>::In* v) { q = load_vec_at<KIND>(v); }
+    __device__ __forceinline__ Q4 get() const { return q; }
+};
 
 template <int KIND>
 __device__ __forceinline__ int64_t head_count(const typename IK<KIND>::In* rowp, int64_t N) {
@@ -196,16 +239,16 @@ __global__ void __launch_bounds__(CTA) intlse_rows_kernel(
         const In* p = vbase + 4 * (int64_t)t;  // chain t's vector in round 0
         constexpr int64_t kRound = 4 * 256;    // elements per round
         {
-            Q4 buf[D];
+            RoundBuf<KIND, (D > 4)> buf[D];
 #pragma unroll
             for (int d = 0; d < D; ++d)
-                if (1 + d < Kf) buf[d] = load_vec_at<KIND>(p + (1 + d) * kRound);
+                if (1 + d < Kf) buf[d].load(p + (1 + d) * kRound);
             int64_t k = 1;
             for (; k + 2 * D <= Kf; k += D) {  // every load of the block is a full round
 #pragma unroll
                 for (int d = 0; d < D; ++d) {
-                    const Q4 cur = buf[d];
-                    buf[d] = load_vec_at<KIND>(p + (k + d + D) * kRound);
+                    const Q4 cur = buf[d].get();
+                    buf[d].load(p + (k + d + D) * kRound);
 #pragma unroll
                     for (int e = 0; e < 4; ++e) acc = pair_exact<F, LUT>(acc, cur.v[e], lut);
                 }
@@ -214,8 +257,8 @@ __global__ void __launch_bounds__(CTA) intlse_rows_kernel(
 #pragma unroll
                 for (int d = 0; d < D; ++d) {
                     if (k + d < Kf) {
-                        const Q4 cur = buf[d];
-                        if (k + d + D < Kf) buf[d] = load_vec_at<KIND>(p + (k + d + D) * kRound);
+                        const Q4 cur = buf[d].get();
+                        if (k + d + D < Kf) buf[d].load(p + (k + d + D) * kRound);
 #pragma unroll
                         for (int e = 0; e < 4; ++e) acc = pair_exact<F, LUT>(acc, cur.v[e], lut);
                     }
@@ -282,7 +325,7 @@ __global__ void __launch_bounds__(256) intlse_whole_rounds_kernel(
     const typename IK<KIND>::In* vp = x + row * N + 4 * t;
     Q4 q[K];
 #pragma unroll
-    for (int k = 0; k < K; ++k) q[k] = load_vec_at<KIND>(vp + k * 1024);
+    for (int k = 0; k < K; ++k) q[k] = load_vec_at<KIND>(vp + k * 1024);  // all in flight at once
     if constexpr (LUT) fill_lane_lut<256>(lut_s, F == 16 ? kLutQ16 : kLutQ10_6);
     __syncthreads();
     const LaneLut lut{lut_s, lane};
