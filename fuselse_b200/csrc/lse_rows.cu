@@ -26,6 +26,7 @@
 #include <cuda_fp16.h>
 #include <algorithm>
 #include <cstdlib>
+#include <type_traits>
 
 namespace cg = cooperative_groups;
 
@@ -143,6 +144,23 @@ __global__ void __launch_bounds__(kThreads) lse_warp_kernel(
     float m, s;
     fold_row_warp(rowp, N, lane, m, s);
     if (lane == 0) write_row<T, MODE>(out, row, m, s, empty_value, tg, sel);
+}
+
+// Warp-sized rows on the balanced schedule (fold_rows_flat, rows.cuh): one
+// CTA per SM, every warp the same number of vectors.
+template <typename T, int MODE>
+__global__ void __launch_bounds__(kFlatThreads, 1) lse_flat_kernel(
+    const T* __restrict__ x, float* __restrict__ out, int64_t B, int64_t N, float empty_value) {
+    static_assert(MODE != kOutSelect, "the selective output keeps one warp per row");
+    extern __shared__ float2 part[];
+    pdl_wait();
+    pdl_launch_dependents();
+    const FlatShape sh = fold_rows_flat<T>(x, B, N, part);
+    for (int t = threadIdx.x; t < sh.nr; t += kFlatThreads) {
+        float m, s;
+        flat_row_state(part, sh, t, m, s);
+        write_row<T, MODE>(out, sh.r0 + t, m, s, empty_value, Target<T>{}, SelArgs{});
+    }
 }
 
 __global__ void lse_combine_kernel(const float2* __restrict__ ms, float* __restrict__ out,
@@ -285,8 +303,26 @@ template <typename T, int MODE>
 int launch_rows(const T* x, float* out, int64_t B, int64_t N, float empty_value,
                 cudaStream_t stream, const char* what, SelArgs sel = SelArgs{},
                 RowMap rm = RowMap{INT64_MAX, 0, -1}) {
-    if (rm.row_stride < 0) rm = RowMap::dense(N);
+    const bool dense = rm.row_stride < 0;
+    if (dense) rm = RowMap::dense(N);
     if (warp_per_row<T>(B, N)) {
+        // fp16 rows only: fp32 rows keep 48 warps per SM one warp per row, 32
+        // on the flat schedule (measured 1-2 % slower at (16384, 4096))
+        if constexpr (MODE != kOutSelect && std::is_same<T, __half>::value) {
+            const int64_t grid = std::min<int64_t>(B, sm_count());
+            size_t smem = 0;
+            static std::atomic<int> warp_ctas{0};
+            if (dense && flat_rows_ok<T>(x, B, N, grid, &smem) &&
+                short_last_wave(B, resident_row_warps(lse_warp_kernel<T, MODE>, kThreads, warp_ctas))) {
+                auto kern = lse_flat_kernel<T, MODE>;
+                if (smem > 48 * 1024)
+                    FL_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)kFlatSmemMax));
+                LaunchCfg lc(dim3((unsigned)grid), dim3(kFlatThreads), smem, stream);
+                FL_CUDA(cudaLaunchKernelEx(&lc.cfg, kern, x, out, B, N, empty_value));
+                return check_launch(what);
+            }
+        }
         const int64_t grid = (B + kWarps - 1) / kWarps;
         FL_REQUIRE(grid <= INT32_MAX, "%s: B=%lld too large", what, (long long)B);
         LaunchCfg lc(dim3((unsigned)grid), dim3(kThreads), 0, stream);

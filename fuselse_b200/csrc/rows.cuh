@@ -228,6 +228,148 @@ __device__ __forceinline__ void ms_block_reduce(float& m, float& s) {
     }
 }
 
+// Balanced ("flat") schedule for many warp-sized rows.  One warp per row
+// leaves the last wave of rows partly empty whenever B is not a multiple of the
+// resident warps (8192 rows of 32 KB on 148 SMs x 32 warps: 1.73 waves, the
+// second 73 % full).  Here one CTA of kFlatWarps warps runs on each SM; CTA c
+// takes rows [c*B/grid, (c+1)*B/grid) (the CTAs' row counts differ by one at
+// most), and its warps split those rows' 16-byte vectors, taken in row-major
+// order, into equal contiguous ranges, so every warp of the grid streams the
+// same number of bytes to within one row per CTA.  A warp's range crosses a few
+// row boundaries; at each it leaves the piece's (m, s) in shared memory, in the
+// row's slot for that warp (warp - the row's first warp), and flat_row_state
+// merges a row's pieces, in warp order, after the barrier that ends
+// fold_rows_flat.  Rows must start 16-byte aligned and be a whole number of
+// vectors long; flat_rows_ok checks the sizes.
+constexpr int kFlatWarps = 32;
+constexpr int kFlatThreads = kFlatWarps * 32;
+
+struct FlatShape {
+    int64_t r0;  // first row of this CTA
+    int nr;      // rows of this CTA
+    int nv;      // vectors per row
+    int F;       // vectors of this CTA (nr * nv)
+    int slots;   // piece slots per row
+};
+
+// Slots a row needs when nr rows of nv vectors are split over kFlatWarps
+// ranges (lengths floor or ceil of nr*nv/kFlatWarps): a row meets at most
+// ceil(nv / shortest range) + 1 of them.
+__host__ __device__ inline int flat_slots(int64_t nr, int64_t nv) {
+    const int64_t range = nr * nv / kFlatWarps;  // shortest range
+    if (range < 1) return kFlatWarps;
+    const int64_t k = (nv + range - 1) / range + 1;
+    return static_cast<int>(k < kFlatWarps ? k : kFlatWarps);
+}
+
+__device__ __forceinline__ FlatShape flat_shape(int64_t B, int64_t N, int E) {
+    FlatShape sh;
+    sh.r0 = (int64_t)blockIdx.x * B / gridDim.x;
+    sh.nr = static_cast<int>((int64_t)(blockIdx.x + 1) * B / gridDim.x - sh.r0);
+    sh.nv = static_cast<int>(N / E);
+    sh.F = sh.nr * sh.nv;
+    sh.slots = flat_slots(B / gridDim.x, sh.nv);  // the fewest rows give the shortest ranges
+    return sh;
+}
+
+// First vector of warp w's range.
+__device__ __forceinline__ int flat_begin(int F, int w) {
+    return static_cast<int>((int64_t)F * w / kFlatWarps);
+}
+
+// part: shared memory of nr * slots float2.
+template <typename T>
+__device__ __forceinline__ FlatShape fold_rows_flat(const T* __restrict__ x, int64_t B, int64_t N,
+                                                    float2* part) {
+    constexpr int E = Elem<T>::kPerVec;
+    const FlatShape sh = flat_shape(B, N, E);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int i = threadIdx.x; i < sh.nr * sh.slots; i += kFlatThreads)
+        part[i] = make_float2(-INFINITY, 0.0f);
+    __syncthreads();
+    int f = flat_begin(sh.F, warp);
+    const int f1 = flat_begin(sh.F, warp + 1);
+    const T* xr = x + sh.r0 * N;
+    while (f < f1) {
+        const int rl = f / sh.nv;
+        const int v0 = f - rl * sh.nv;
+        const int v1 = min(sh.nv, v0 + (f1 - f));
+        float m = -INFINITY, s = 0.0f;
+        fold_vectors<T, FwdShape<T>::kWarpU, FwdShape<T>::kWarpPipe>(xr + (int64_t)rl * N, v0, v1,
+                                                                      lane, 32, m, s);
+        ms_warp_allreduce(m, s);
+        if (lane == 0) {
+            // the row's first warp: the last w whose range starts at or before the row
+            const int fr = rl * sh.nv;
+            int w0 = static_cast<int>((int64_t)fr * kFlatWarps / sh.F);
+            while (w0 + 1 < kFlatWarps && flat_begin(sh.F, w0 + 1) <= fr) ++w0;
+            while (w0 > 0 && flat_begin(sh.F, w0) > fr) --w0;
+            part[rl * sh.slots + (warp - w0)] = make_float2(m, s);
+        }
+        f += v1 - v0;
+    }
+    __syncthreads();
+    return sh;
+}
+
+// State of local row t of the CTA: its pieces merged in warp order.
+__device__ __forceinline__ void flat_row_state(const float2* part, const FlatShape& sh, int t,
+                                               float& m, float& s) {
+    m = part[t * sh.slots].x;
+    s = part[t * sh.slots].y;
+    for (int k = 1; k < sh.slots; ++k) ms_merge(m, s, part[t * sh.slots + k].x, part[t * sh.slots + k].y);
+}
+
+// Whether the flat schedule can take a (B, N) operand of T at x on a grid of
+// `grid` CTAs, and its shared-memory bytes: dense rows of at least 4 KB
+// (shorter rows keep one warp each: their grids are latency-bound and have no
+// long last wave), 16-byte aligned, a CTA's vectors within 32-bit offsets and
+// its piece slots within kFlatSmemMax.  FL_FLAT_ROWS 0 turns the schedule off.
+#ifndef FL_FLAT_ROWS
+#define FL_FLAT_ROWS 1
+#endif
+constexpr int64_t kFlatSmemMax = 96 * 1024;
+template <typename T>
+inline bool flat_rows_ok(const void* x, int64_t B, int64_t N, int64_t grid, size_t* smem) {
+    const int64_t bytes = N * (int64_t)sizeof(T);
+    if (!(FL_FLAT_ROWS && grid > 0 && B >= grid && bytes >= 4096 && bytes % 16 == 0 &&
+          aligned_to(x, 16)))
+        return false;
+    const int64_t nr = (B + grid - 1) / grid, nv = bytes / 16;
+    if (nr * nv > INT32_MAX) return false;
+    const int64_t need = nr * flat_slots(B / grid, nv) * (int64_t)sizeof(float2);
+    if (need > kFlatSmemMax) return false;
+    *smem = static_cast<size_t>(need);
+    return true;
+}
+
+// Whether one warp per row would leave a short last wave (at most half of the
+// `resident` warps busy): only then does the flat schedule pay for its row
+// pieces.  Measured on B200 for (B, 16032) fp16 shard partials, flat against
+// one warp per row: 1.11x faster at 1.25 waves, 1.05x at 1.5, 1.07x at 2.11,
+// 1.03x at 2.5; 0.98x at 1.73 waves and at whole waves.  FL_FLAT_ROWS 2 takes
+// the flat schedule whatever the waves.
+inline bool short_last_wave(int64_t B, int64_t resident) {
+    if (FL_FLAT_ROWS == 2) return true;
+    const int64_t rem = resident > 0 ? B % resident : 0;
+    return rem != 0 && 2 * rem <= resident;
+}
+
+// Warps of a one-warp-per-row kernel resident on the current device; the
+// per-SM CTA count (a property of the kernel's build) is kept in `cache`.
+template <typename K>
+inline int64_t resident_row_warps(K kernel, int threads, std::atomic<int>& cache) {
+    int per_sm = cache.load(std::memory_order_relaxed);
+    if (per_sm == 0) {
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0) !=
+                cudaSuccess ||
+            per_sm < 1)
+            per_sm = 1;
+        cache.store(per_sm, std::memory_order_relaxed);
+    }
+    return (int64_t)per_sm * (threads / 32) * sm_count();
+}
+
 // One warp folds a whole row (head elements, 16-byte vectors, tail elements);
 // every lane ends with the row's state.
 template <typename T>

@@ -81,6 +81,30 @@ __global__ void __launch_bounds__(kRowsPerCta * 32) vocab_scatter_kernel(
     }
 }
 
+// The same exchange on the balanced schedule (fold_rows_flat, rows.cuh), for
+// aligned rows of at least 4 KB: one CTA per SM whose warps all fold the same
+// number of vectors; each CTA delivers its rows' pairs once their pieces are
+// merged (threads over rows x ranks).
+template <typename T>
+__global__ void __launch_bounds__(kFlatThreads, 1) vocab_scatter_flat_kernel(
+    const T* __restrict__ x, int64_t B, int64_t N, unsigned char* const* __restrict__ peers,
+    unsigned char* __restrict__ local, int rank, int G) {
+    extern __shared__ float2 part[];
+    uint32_t* header = reinterpret_cast<uint32_t*>(local);
+    const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(header) + 1;
+    const int64_t slot = epoch & 1u;
+    if (blockIdx.x == 0 && threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(header + 2) = epoch;
+    const FlatShape sh = fold_rows_flat<T>(x, B, N, part);
+    for (int i = threadIdx.x; i < sh.nr * G; i += kFlatThreads) {
+        const int t = i / G, p = i - t * G;
+        float m, s;
+        flat_row_state(part, sh, t, m, s);
+        float2* dst = reinterpret_cast<float2*>(peers[p] + pairs_offset(G)) +
+                      ((slot * G + rank) * B + sh.r0 + t);
+        *dst = make_float2(m, s);
+    }
+}
+
 constexpr int kCombineThreads = 256;
 constexpr int64_t kDefaultWaitNs = 2000000000LL;  // 2 s
 constexpr uint32_t kWaitLimitIters = 1u << 26;
@@ -151,13 +175,45 @@ int launch_exchange(const void* x, int dtype, int64_t B, int64_t N, unsigned cha
                     unsigned char* local, int rank, int G, float* out, uint64_t wait_ns,
                     cudaStream_t s, const char* what) {
     const int64_t ngroups = (B + kRowsPerCta - 1) / kRowsPerCta;
-    LaunchCfg sc(dim3((unsigned)ngroups), dim3(kRowsPerCta * 32), 0, s, /*pdl=*/false);
-    if (dtype == 0)
-        FL_CUDA(cudaLaunchKernelEx(&sc.cfg, vocab_scatter_kernel<float>,
-                                   reinterpret_cast<const float*>(x), B, N, peers, local, rank, G));
-    else
-        FL_CUDA(cudaLaunchKernelEx(&sc.cfg, vocab_scatter_kernel<__half>,
-                                   reinterpret_cast<const __half*>(x), B, N, peers, local, rank, G));
+    const int64_t fgrid = B < sm_count() ? B : sm_count();
+    size_t fsmem = 0;
+    // flat for rows longer than the lse path gives one warp
+    // (FwdShape::kWarpRowBytes), and for fp16 rows whose one-warp-per-row grid
+    // would leave a short last wave
+    static std::atomic<int> warp_ctas{0};
+    bool flat;
+    if (dtype == 0) {
+        flat = N * 4 > FwdShape<float>::kWarpRowBytes && flat_rows_ok<float>(x, B, N, fgrid, &fsmem);
+    } else {
+        flat = flat_rows_ok<__half>(x, B, N, fgrid, &fsmem) &&
+               (N * 2 > FwdShape<__half>::kWarpRowBytes ||
+                short_last_wave(B, resident_row_warps(vocab_scatter_kernel<__half>, kRowsPerCta * 32,
+                                                      warp_ctas)));
+    }
+    if (flat) {
+        LaunchCfg fc(dim3((unsigned)fgrid), dim3(kFlatThreads), fsmem, s, /*pdl=*/false);
+        if (dtype == 0) {
+            if (fsmem > 48 * 1024)
+                FL_CUDA(cudaFuncSetAttribute(vocab_scatter_flat_kernel<float>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFlatSmemMax));
+            FL_CUDA(cudaLaunchKernelEx(&fc.cfg, vocab_scatter_flat_kernel<float>,
+                                       reinterpret_cast<const float*>(x), B, N, peers, local, rank, G));
+        } else {
+            if (fsmem > 48 * 1024)
+                FL_CUDA(cudaFuncSetAttribute(vocab_scatter_flat_kernel<__half>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFlatSmemMax));
+            FL_CUDA(cudaLaunchKernelEx(&fc.cfg, vocab_scatter_flat_kernel<__half>,
+                                       reinterpret_cast<const __half*>(x), B, N, peers, local, rank, G));
+        }
+    } else {
+        LaunchCfg sc(dim3((unsigned)ngroups), dim3(kRowsPerCta * 32), 0, s, /*pdl=*/false);
+        if (dtype == 0)
+            FL_CUDA(cudaLaunchKernelEx(&sc.cfg, vocab_scatter_kernel<float>,
+                                       reinterpret_cast<const float*>(x), B, N, peers, local, rank, G));
+        else
+            FL_CUDA(cudaLaunchKernelEx(&sc.cfg, vocab_scatter_kernel<__half>,
+                                       reinterpret_cast<const __half*>(x), B, N, peers, local, rank, G));
+    }
     if (int st = check_launch(what)) return st;
     const int64_t cgrid = (B + kCombineThreads - 1) / kCombineThreads;
     LaunchCfg cc(dim3((unsigned)cgrid), dim3(kCombineThreads), 0, s, /*pdl=*/false);
