@@ -36,7 +36,9 @@ constexpr int kThreads = 256;
 // is what L2 should hold while every parent gathers from it; wider tiles also
 // make each gathered child chunk longer (cols x 4 B contiguous).  On B200 the
 // chunk length wins: fp32 layer at P=262144, S=65536, E=32, batch 512 took
-// 1.31 / 0.70 / 0.50 / 0.497 ms with 16 / 32 / 64 / 128-column tiles.
+// 1.31 / 0.70 / 0.50 / 0.497 ms with 16 / 32 / 64 / 128-column tiles, and with
+// the staged edges at an odd row stride (no bank conflicts between the nodes
+// of a warp) 0.695 / 0.490 / 0.483 ms at 32 / 64 / 128 columns.
 #ifndef FL_SPARSE_TILE
 #define FL_SPARSE_TILE 128
 #endif
@@ -168,13 +170,16 @@ struct SparseArgs {
     int64_t num_out;  // num_nblocks * block_size
     int64_t batch;
     int E;
+    int EP;  // staged row stride in words: E rounded up to odd
     int block_size;
     int64_t nodes_per_cta;
     int* err;
 };
 
-// Shared memory: [nodes_per_cta][E] child ids (int32), then log-weights, then
-// per-node flags (bad index, output row).
+// Shared memory: [nodes_per_cta][EP] child ids (int32), then log-weights, then
+// per-node flags (bad index, output row).  The odd row stride EP puts the
+// edge-e words of the several nodes a warp serves (narrow tiles) in distinct
+// banks.
 template <bool Q16, int VEC, int ET>
 __global__ void __launch_bounds__(kThreads) sparse_kernel(SparseArgs A) {
     constexpr int TPN = kTileCols / VEC;  // threads per node within a tile
@@ -186,11 +191,11 @@ __global__ void __launch_bounds__(kThreads) sparse_kernel(SparseArgs A) {
     const int64_t n1 = min(A.num_out, n0 + A.nodes_per_cta);
     if (n0 >= n1) return;
     const int nn = static_cast<int>(n1 - n0);
-    const int E = A.E;
+    const int E = A.E, EP = A.EP;
     int* s_cid = reinterpret_cast<int*>(smem);
-    float* s_lw = reinterpret_cast<float*>(s_cid + (size_t)nn * E);
+    float* s_lw = reinterpret_cast<float*>(s_cid + (size_t)nn * EP);
     long long* s_row = reinterpret_cast<long long*>(
-        smem + (((size_t)nn * E * 8 + 15) & ~(size_t)15));  // output row, or -1 (skip), flag in bit 62
+        smem + (((size_t)nn * EP * 8 + 15) & ~(size_t)15));  // output row, or -1 (skip), flag in bit 62
 
     if constexpr (Q16) fill_lane_lut<kThreads>(lut_s, kLutQ16);
     // stage edges of [n0, n1)
@@ -202,10 +207,10 @@ __global__ void __launch_bounds__(kThreads) sparse_kernel(SparseArgs A) {
         const int64_t cid = A.cids[nb * E + e];
         const int64_t pid = A.pids[nb * E + e] + p;
         const bool ok = cid >= 0 && cid < A.num_elements && pid >= 0 && pid < A.num_params;
-        s_cid[i] = ok ? static_cast<int>(cid) : -1;
+        s_cid[(size_t)ln * EP + e] = ok ? static_cast<int>(cid) : -1;
         // fp32 stages lw * log2(e) (its logits are formed as x * log2(e) + that);
         // Q16.16 keeps lw, the reference's conversion input being x + lw
-        s_lw[i] = ok ? (Q16 ? log_weight(__ldg(A.params + pid))
+        s_lw[(size_t)ln * EP + e] = ok ? (Q16 ? log_weight(__ldg(A.params + pid))
                             : log_weight(__ldg(A.params + pid)) * kLog2e) : 0.0f;
     }
     for (int ln = threadIdx.x; ln < nn; ln += kThreads) {
@@ -217,7 +222,7 @@ __global__ void __launch_bounds__(kThreads) sparse_kernel(SparseArgs A) {
     __syncthreads();
     for (int ln = threadIdx.x; ln < nn; ln += kThreads) {
         bool bad = s_row[ln] < 0;
-        for (int e = 0; e < E && !bad; ++e) bad = s_cid[(size_t)ln * E + e] < 0;
+        for (int e = 0; e < E && !bad; ++e) bad = s_cid[(size_t)ln * EP + e] < 0;
         if (bad && A.err) *A.err = 1;
         if (bad && s_row[ln] >= 0) s_row[ln] |= (1LL << 62);
     }
@@ -243,8 +248,8 @@ __global__ void __launch_bounds__(kThreads) sparse_kernel(SparseArgs A) {
                 for (int c = 0; c < VEC; ++c) outp[c] = __int_as_float(0x7fc00000);
                 continue;
             }
-            const int* cp = s_cid + (size_t)ln * E;
-            const float* wp = s_lw + (size_t)ln * E;
+            const int* cp = s_cid + (size_t)ln * EP;
+            const float* wp = s_lw + (size_t)ln * EP;
             Acc<Q16, VEC, ET> acc;
             acc.init();
             // one group of kGroup edges; nvalid < kGroup only for the tail group
@@ -338,12 +343,13 @@ int sparse_entry(float* node_mars, const float* em, const float* params, const i
     a.num_out = num_nblocks * block_size;
     a.batch = batch;
     a.E = static_cast<int>(E);
+    a.EP = static_cast<int>(E | 1);
     a.block_size = static_cast<int>(block_size);
     a.err = err;
     FL_REQUIRE(block_size <= INT32_MAX, "%s: block_size too large", what);
 
     // persistent grid: 4 CTAs per SM, more if the staged edges would not fit
-    const int64_t per_node = E * 8;
+    const int64_t per_node = (E | 1) * 8;
     int64_t grid = 4LL * sm_count();
     int64_t npc = (a.num_out + grid - 1) / grid;
     if (npc * per_node + npc * 8 + 16 > kMetaBudget) {
