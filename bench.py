@@ -27,7 +27,9 @@ finds its input left in L2 by the step before (`--same-input`: one batch);
   * per-kernel pass (`kernels`, `roofline`): each kernel replayed from its own
     graph with CUDA events between the kernels (`ms_per_step_kernel_pass` is
     their sum; `--kernel-graphs` reports it as the step, `--eager` launches
-    directly).
+    directly).  `kernels.fwd.alone` times the forward again on its own (a
+    graph per call, inputs alternating): inside the step it also carries the
+    write-back of the backward's last dirty gradient lines.
 Barrier and synchronize around each timed region; max over ranks.
 
 `e2e` (default workload): the same metric through the public host-buffer API
@@ -960,6 +962,20 @@ def main():
 
     extra = {}
     if args.workload == "fwdbwd_f32" and not args.no_extra:
+        # the forward kernel timed on its own (a graph per call, the two input
+        # batches alternating): inside the step it also pays the write-back of
+        # the backward's last gradient lines, still dirty in L2 when it starts
+        wf = FwdBwdF32(dev, seed=rank, do_bwd=False)
+        f_ms = max_over_ranks(run_step_graphs(wf, args.steps, args.warmup, dev, dist_on), dist_on, dev)
+        del wf
+        torch.cuda.empty_cache()
+        fb = ks[0][2]
+        kernels["fwd"]["in_step"] = ("inside the step the forward also writes back the backward's "
+                                     "last gradient lines (~54 MB left dirty in L2)")
+        kernels["fwd"]["alone"] = {"ms": f_ms, "GB_s": fb / (f_ms * 1e-3) / 1e9,
+                                   "frac_of_peak": fb / (f_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                                   "how": "forward only, one graph per call, two input batches "
+                                          "alternating, same run"}
         extra["strong"] = strong_record(dev, world, rank, args.steps, args.warmup, dist_on, step_ms)
         extra["vocab_exchange"] = vocab_exchange_record(dev, world, rank, args.steps, args.warmup,
                                                         dist_on)
