@@ -5,7 +5,10 @@
 //   kernel 1 (vocab_scatter_kernel): one warp per row folds the local columns
 //     into (m, s) = (max, sum exp(x - m)) and stores the pair straight into
 //     every rank's exchange buffer (P2P stores through CUDA IPC peer
-//     mappings).  It has no epilogue: no fence, no counter.
+//     mappings).  It has no epilogue: no fence, no counter.  Rows longer than
+//     one warp takes, and fp16 rows whose one-warp-per-row grid would end in a
+//     short last wave, go through vocab_scatter_flat_kernel instead (the
+//     balanced schedule of rows.cuh), which stores the same pairs.
 //   kernel 2 (vocab_combine_kernel, one thread per row): with G > 1 every CTA
 //     first publishes — threads 0..G-1 store the call's epoch into this rank's
 //     flag word of every rank's buffer (release, system scope).  Kernel 1 finished
