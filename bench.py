@@ -724,7 +724,7 @@ def copy_floor(wl, steps, dev, dist_on):
     input from pinned host memory to the device on one stream while a device
     buffer of the output's size goes back to pinned host memory on another,
     every rank at once (the GPUs share the host's memory and PCIe root) — no
-    kernel.  Returns ms per step."""
+    kernel.  Returns ms per step: the fastest of `steps` timed repetitions."""
     dst = torch.empty_like(wl.x)
     up, down = torch.cuda.Stream(), torch.cuda.Stream()
     cur = torch.cuda.current_stream()
@@ -739,21 +739,24 @@ def copy_floor(wl, steps, dev, dist_on):
         cur.wait_stream(up)
         cur.wait_stream(down)
 
-    once()
+    for _ in range(2):
+        once()
     torch.cuda.synchronize()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
     if dist_on:
         torch.distributed.barrier()
     torch.cuda.synchronize()
-    s.record()
-    for _ in range(steps):
+    evs[0].record()
+    for i in range(steps):
         once()
-    e.record()
+        evs[i + 1].record()
     torch.cuda.synchronize()
     if dist_on:
         torch.distributed.barrier()
     del dst
-    return s.elapsed_time(e) / steps
+    # a bound: the fastest of the timed copies (one slow copy, e.g. a host page
+    # fault or another tenant on the link, does not lower the floor)
+    return min(evs[i].elapsed_time(evs[i + 1]) for i in range(steps))
 
 
 def max_over_ranks(v, dist_on, dev):
@@ -983,7 +986,7 @@ def main():
     e2e = None
     if not args.no_e2e and hasattr(wl, "e2e_step"):
         e2e_ms = max_over_ranks(run_e2e(wl, max(3, args.steps // 4), 3, dev, dist_on), dist_on, dev)
-        floor_ms = max_over_ranks(copy_floor(wl, 3, dev, dist_on), dist_on, dev)
+        floor_ms = max_over_ranks(copy_floor(wl, 6, dev, dist_on), dist_on, dev)
         e2e = {"value": world * bytes_step / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
                "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h, "ms_per_step": e2e_ms,
                "api": getattr(wl, "e2e_api", "public API"),
